@@ -1,0 +1,190 @@
+// Kernel-side data structures and host launch wrappers shared by the planner.
+#pragma once
+#include <cuda_runtime.h>
+#include <cstdint>
+#include <cstddef>
+
+namespace tg {
+
+enum DType : int { F32 = 0, I32 = 1, BOOL = 2 };
+
+int device_sm_count();
+
+// ---------------------------------------------------------------------------
+// Elementwise program ("EW"): one kernel evaluates a straight-line program of
+// elementwise IR ops over every element of a common output shape. Inputs are
+// read through broadcast index maps; several program values can be stored.
+// A single op is a one-instruction program; the fusion pass merges chains of
+// same-shape elementwise ops into one program so intermediates stay in
+// registers instead of round-tripping HBM.
+// ---------------------------------------------------------------------------
+constexpr int EW_MAX_IN = 8;
+constexpr int EW_MAX_OUT = 4;
+constexpr int EW_MAX_INSTR = 40;
+constexpr int EW_MAX_RANK = 6;
+constexpr int EW_NREG = 8;
+
+enum EwInMode : int {
+  IN_FULL = 0,     // same shape as output, contiguous: offset = i
+  IN_SCALAR = 1,   // one element: offset = 0
+  IN_PERIOD = 2,   // trailing-suffix broadcast: offset = i % period
+  IN_ROWDIV = 3,   // leading-prefix broadcast ([..., 1] over [..., D]): offset = i / period
+  IN_STRIDED = 4,  // general: offset = sum(coord_d * stride_d)
+};
+
+struct EwInput {
+  const void* ptr;
+  int mode;
+  int dtype;
+  int64_t period;
+  int64_t strides[EW_MAX_RANK];
+};
+
+enum EwOp : uint8_t {
+  EW_LOAD = 0,  // dst <- input[a]
+  EW_ADD, EW_SUB, EW_MUL, EW_DIV, EW_MIN, EW_MAX,
+  EW_MULS, EW_ADDS,  // dst <- a (*|+) imm
+  EW_SQRT, EW_RSQRT, EW_LOG, EW_EXP, EW_RELU, EW_NEG, EW_ABS, EW_TANH, EW_SIGMOID, EW_ERF,
+  EW_SIN, EW_COS,
+  EW_LESS, EW_GREATER,    // dst <- (a op b) ? 1 : 0 as int bits (aux=1: compare as i32)
+  EW_WHERE,               // dst <- a(int bits) != 0 ? b : c   (bits preserved)
+  EW_RELU_GRAD,           // dst <- a > 0 ? b : 0
+  EW_DROPOUT,             // dst <- a * mask(seed, salt=aux, i); imm = f32(p), imm2 = f32(scale)
+  EW_WHERE_CAUSAL,        // dst <- (k <= q) ? a : imm ; aux = T
+  EW_ADAM_M,              // dst <- imm*a + imm2*b
+  EW_ADAM_V,              // dst <- imm*a + imm2*b*b
+  EW_ADAM_P,              // dst <- d*a - (c*b)/(sqrt(e)+imm)  a=p b=m c=lrt d=shrink e=v
+  EW_COPY,                // dst <- a
+  EW_CONST,               // dst <- imm (bits from aux when c==1)
+};
+
+struct EwInstr {
+  uint8_t op, dst, a, b, c, d, e, pad;
+  float imm, imm2;
+  uint32_t aux;
+};
+
+struct EwProgram {
+  int64_t numel;
+  int rank;
+  int n_in, n_out, n_instr;
+  int64_t dims[EW_MAX_RANK];
+  EwInput in[EW_MAX_IN];
+  void* out[EW_MAX_OUT];
+  uint8_t out_reg[EW_MAX_OUT];
+  const int* seed;      // __prngSeed device scalar (dropout)
+  int64_t drop_offset;  // global element offset of this shard (data parallel)
+  int vec4;             // all inputs/outputs allow 4-wide access
+  EwInstr code[EW_MAX_INSTR];
+};
+
+void launch_ew(const EwProgram& p, cudaStream_t s);
+
+// ---------------------------------------------------------------------------
+// Row kernels: reductions and softmaxes along the last axis.
+// ---------------------------------------------------------------------------
+enum RowKind : int { ROW_SUM = 0, ROW_MEAN, ROW_ARGMAX, ROW_LOGSOFTMAX, ROW_SOFTMAX_CAUSAL, ROW_CATEGORICAL };
+// x: [rows, D] contiguous. For ROW_SUM/MEAN/ARGMAX/CATEGORICAL out has `rows`
+// elements; for softmaxes out is [rows, D]. For softmax_causal, row r is
+// query position r % D.
+void launch_row(int kind, const float* x, void* out, int64_t rows, int64_t D, cudaStream_t s,
+                const int* seed = nullptr, uint32_t salt = 0, float* scratch = nullptr,
+                size_t scratch_floats = 0);
+// Scratch floats launch_row uses (long-row split path); 0 when none.
+size_t row_scratch_floats(int kind, int64_t rows, int64_t D);
+
+// Column sums [outer, inner] -> [inner] (deterministic two-pass with scratch).
+size_t colsum_scratch_floats(int64_t outer, int64_t inner);
+void launch_colsum(const float* x, float* out, int64_t outer, int64_t inner, float* scratch, cudaStream_t s);
+// General sum-to-shape: keep[d] = 1 where the output keeps input axis d.
+void launch_sum_general(const float* x, float* out, int rank, const int64_t* in_dims, const int64_t* keep,
+                        int64_t in_numel, int64_t out_numel, cudaStream_t s);
+
+// ---------------------------------------------------------------------------
+// Strided copy: out[sum c*out_strides] = in[sum c*in_strides] over dims.
+// Covers permute, slice_range, concat pieces, scatter_axis, broadcast copies.
+// ---------------------------------------------------------------------------
+constexpr int CP_MAX_RANK = 8;
+struct CopyDesc {
+  int rank;
+  int64_t dims[CP_MAX_RANK];
+  int64_t in_strides[CP_MAX_RANK];
+  int64_t out_strides[CP_MAX_RANK];
+  int64_t numel;
+};
+void launch_copy(const CopyDesc& d, const void* in, void* out, cudaStream_t s);
+void launch_fill(void* out, int64_t n, uint32_t bits, cudaStream_t s);
+void launch_arange(void* out, int64_t n, int dtype, cudaStream_t s);
+void launch_one_hot(const int* idx, void* out, int64_t n_idx, int64_t depth, int dtype, cudaStream_t s);
+void launch_randn(float* out, int64_t n, const int* seed, uint32_t salt_const, cudaStream_t s);
+
+// ---------------------------------------------------------------------------
+// GEMM: C[b] (+)= alpha * A[b] @ B[b] (+ bias) with arbitrary strides.
+// ---------------------------------------------------------------------------
+struct GemmDesc {
+  int64_t M, N, K, batch;
+  const float* A; int64_t lda_m, lda_k, a_batch;  // A(m,k) = A[m*lda_m + k*lda_k]
+  const float* B; int64_t ldb_k, ldb_n, b_batch;  // B(k,n) = B[k*ldb_k + n*ldb_n]
+  float* C; int64_t ldc, c_batch;                 // C(m,n) = C[m*ldc + n]
+  const float* bias;                              // optional [N], added in the epilogue
+  float alpha;
+  int accumulate;                                 // C += result
+};
+void launch_gemm_simt(const GemmDesc& g, cudaStream_t s);
+// tcgen05/TMEM 3xTF32 GEMM; returns false when the shape/layout is not taken.
+bool launch_gemm_tc(const GemmDesc& g, cudaStream_t s);
+
+// Embedding gather: out[r, :] = table[idx[r], :] (0 where idx out of range).
+void launch_gather_rows(const int* idx, const float* table, float* out, int64_t rows, int64_t V,
+                        int64_t D, cudaStream_t s);
+// Deterministic embedding backward: dtable[v,:] = sum of dy[r,:] over rows r
+// with idx[r]==v, in ascending r (stable counting sort, no float atomics).
+size_t embedding_grad_scratch_ints(int64_t rows, int64_t V);
+void launch_embedding_grad(const int* idx, const float* dy, float* dtable, int64_t rows, int64_t V,
+                           int64_t D, int* scratch, cudaStream_t s);
+// Row pick: out[r] = x[r, t[r]] (0 if out of range)
+void launch_pick(const float* x, const int* t, float* out, int64_t rows, int64_t V, cudaStream_t s);
+
+// ---------------------------------------------------------------------------
+// conv2d / pool (NCHW)
+// ---------------------------------------------------------------------------
+struct ConvDesc {
+  int B, Cin, H, W, Cout, kH, kW, Hout, Wout, sH, sW, pH, pW, G;
+};
+void launch_conv2d(const ConvDesc& c, const float* x, const float* w, float* y, cudaStream_t s);
+void launch_conv2d_input_grad(const ConvDesc& c, const float* w, const float* dy, float* dx, cudaStream_t s);
+void launch_conv2d_weight_grad(const ConvDesc& c, const float* x, const float* dy, float* dw, cudaStream_t s);
+void launch_maxpool(const ConvDesc& c, const float* x, float* y, cudaStream_t s);
+void launch_maxpool_grad(const ConvDesc& c, const float* x, const float* dy, float* dx, cudaStream_t s);
+
+// ---------------------------------------------------------------------------
+// Fused multi-tensor Adam/AdamW over flat arenas (in place).
+// Elements [0, n_decay) use `shrink` (device scalar or literal); the rest 1.
+// ---------------------------------------------------------------------------
+struct AdamFlatDesc {
+  float* p; float* m; float* v; const float* g;
+  int64_t n, n_decay;
+  float beta1, one_minus_beta1, beta2, one_minus_beta2, eps;
+  const float* lrt;           // device scalar
+  const float* shrink_dev;    // device scalar or nullptr
+  float shrink_lit;
+  float grad_scale;           // multiplies g (1/world for data-parallel averaging)
+};
+void launch_adam_flat(const AdamFlatDesc& d, cudaStream_t s);
+
+// SGD over flat arenas (in place): g_eff = g*scale (+wd*p for decayed);
+// v = mu*v + g_eff; upd = nesterov ? g_eff + mu*v : v; p -= lr*upd.
+struct SgdFlatDesc {
+  float* p; float* v; const float* g;
+  int64_t n, n_decay;
+  float momentum, wd;
+  int nesterov;
+  const float* lr;
+  float grad_scale;
+};
+void launch_sgd_flat(const SgdFlatDesc& d, cudaStream_t s);
+
+// Scale a flat buffer in place (data-parallel gradient averaging).
+void launch_scale(float* x, int64_t n, float s, cudaStream_t st);
+
+}  // namespace tg

@@ -1,0 +1,369 @@
+// Row kernels: last-axis reductions and softmaxes (reference: src/codegen.ts
+// :333-445 sum/mean/argmax/categorical, :627-689 logSoftmax/softmaxCausal,
+// :907-913 + :1383-1477 sum_to_shape), re-designed for B200.
+//
+// One warp per row when the row fits a warp comfortably (D <= 2048), one
+// 256-thread block per row otherwise; warp-shuffle trees, f32 accumulation.
+// A few very long rows (the loss mean, global-norm sums) split across CTAs
+// into a scratch buffer and finish in a second pass, so the reduction never
+// runs on a single SM. Column sums (bias / LayerNorm-gain gradients) are a
+// deterministic two-pass reduction: chunked partial sums, then a fold.
+#include "kernels.cuh"
+
+namespace tg {
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+// (value, index) max with ties broken toward the lower index.
+__device__ __forceinline__ void warp_argmax(float& v, int& idx) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    float ov = __shfl_xor_sync(0xffffffffu, v, o);
+    int oi = __shfl_xor_sync(0xffffffffu, idx, o);
+    if (ov > v || (ov == v && oi < idx)) { v = ov; idx = oi; }
+  }
+}
+// Online-softmax merge of (max, sum) pairs across a warp.
+__device__ __forceinline__ void warp_online(float& m, float& s) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    float om = __shfl_xor_sync(0xffffffffu, m, o);
+    float os = __shfl_xor_sync(0xffffffffu, s, o);
+    float nm = fmaxf(m, om);
+    float a = (m == -INFINITY) ? 0.f : s * expf(m - nm);
+    float b = (om == -INFINITY) ? 0.f : os * expf(om - nm);
+    m = nm;
+    s = a + b;
+  }
+}
+
+__device__ __forceinline__ uint32_t pcg_r(uint32_t h) {
+  h = h * 747796405u + 2891336453u;
+  h = ((h >> ((h >> 28u) + 4u)) ^ h) * 277803737u;
+  return (h >> 22u) ^ h;
+}
+
+// Gumbel-perturbed logit for categorical sampling (src/codegen.ts:409-445).
+__device__ __forceinline__ float gumbel_val(float v, uint32_t sd, uint32_t salt, int64_t flat) {
+  uint32_t h = pcg_r(sd ^ salt ^ (uint32_t)flat);
+  float u = fmaxf(1.0e-10f, __uint2float_rn(h) * 2.3283064365386963e-10f);
+  return v + (-logf(-logf(u)));
+}
+
+template <int KIND>
+__global__ void __launch_bounds__(256) row_warp_kernel(const float* __restrict__ x, void* __restrict__ out,
+                                                       int64_t rows, int64_t D, const int* seed, uint32_t salt) {
+  int lane = threadIdx.x & 31;
+  int64_t warp = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
+  for (int64_t r = warp; r < rows; r += nwarps) {
+    const float* xr = x + r * D;
+    if (KIND == ROW_SUM || KIND == ROW_MEAN) {
+      float s = 0.f;
+      for (int64_t j = lane; j < D; j += 32) s += xr[j];
+      s = warp_sum(s);
+      if (lane == 0) reinterpret_cast<float*>(out)[r] = KIND == ROW_MEAN ? __fdiv_rn(s, (float)D) : s;
+    } else if (KIND == ROW_ARGMAX || KIND == ROW_CATEGORICAL) {
+      float best = -INFINITY;
+      int bi = 0x7fffffff;
+      uint32_t sd = (KIND == ROW_CATEGORICAL && seed) ? (uint32_t)(*seed) : 0u;
+      for (int64_t j = lane; j < D; j += 32) {
+        float v = xr[j];
+        if (KIND == ROW_CATEGORICAL) v = gumbel_val(v, sd, salt, r * D + j);
+        if (bi == 0x7fffffff || v > best) { best = v; bi = (int)j; }
+      }
+      warp_argmax(best, bi);
+      if (lane == 0) reinterpret_cast<int*>(out)[r] = bi == 0x7fffffff ? 0 : bi;
+    } else {
+      int64_t lim = (KIND == ROW_SOFTMAX_CAUSAL) ? (r % D) + 1 : D;
+      float m = -INFINITY, s = 0.f;
+      for (int64_t j = lane; j < lim; j += 32) {
+        float v = xr[j];
+        if (v > m) { s = (m == -INFINITY) ? 0.f : s * expf(m - v); m = v; }
+        s += expf(v - m);
+      }
+      warp_online(m, s);
+      float* o = reinterpret_cast<float*>(out) + r * D;
+      if (KIND == ROW_LOGSOFTMAX) {
+        float lz = m + logf(s);
+        for (int64_t j = lane; j < D; j += 32) o[j] = xr[j] - lz;
+      } else {
+        for (int64_t j = lane; j < D; j += 32) o[j] = j < lim ? __fdiv_rn(expf(xr[j] - m), s) : 0.f;
+      }
+    }
+  }
+}
+
+template <int KIND>
+__global__ void __launch_bounds__(256) row_block_kernel(const float* __restrict__ x, void* __restrict__ out,
+                                                        int64_t rows, int64_t D, const int* seed, uint32_t salt) {
+  __shared__ float sm_a[8];
+  __shared__ float sm_b[8];
+  __shared__ int sm_i[8];
+  int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+  for (int64_t r = blockIdx.x; r < rows; r += gridDim.x) {
+    const float* xr = x + r * D;
+    if (KIND == ROW_SUM || KIND == ROW_MEAN) {
+      float s = 0.f;
+      for (int64_t j = threadIdx.x; j < D; j += blockDim.x) s += xr[j];
+      s = warp_sum(s);
+      if (lane == 0) sm_a[wid] = s;
+      __syncthreads();
+      if (wid == 0) {
+        s = lane < 8 ? sm_a[lane] : 0.f;
+        s = warp_sum(s);
+        if (lane == 0) reinterpret_cast<float*>(out)[r] = KIND == ROW_MEAN ? __fdiv_rn(s, (float)D) : s;
+      }
+      __syncthreads();
+    } else if (KIND == ROW_ARGMAX || KIND == ROW_CATEGORICAL) {
+      float best = -INFINITY;
+      int bi = 0x7fffffff;
+      uint32_t sd = (KIND == ROW_CATEGORICAL && seed) ? (uint32_t)(*seed) : 0u;
+      for (int64_t j = threadIdx.x; j < D; j += blockDim.x) {
+        float v = xr[j];
+        if (KIND == ROW_CATEGORICAL) v = gumbel_val(v, sd, salt, r * D + j);
+        if (bi == 0x7fffffff || v > best) { best = v; bi = (int)j; }
+      }
+      warp_argmax(best, bi);
+      if (lane == 0) { sm_a[wid] = best; sm_i[wid] = bi; }
+      __syncthreads();
+      if (wid == 0) {
+        best = lane < 8 ? sm_a[lane] : -INFINITY;
+        bi = lane < 8 ? sm_i[lane] : 0x7fffffff;
+        warp_argmax(best, bi);
+        if (lane == 0) reinterpret_cast<int*>(out)[r] = bi == 0x7fffffff ? 0 : bi;
+      }
+      __syncthreads();
+    } else {
+      int64_t lim = (KIND == ROW_SOFTMAX_CAUSAL) ? (r % D) + 1 : D;
+      float m = -INFINITY, s = 0.f;
+      for (int64_t j = threadIdx.x; j < lim; j += blockDim.x) {
+        float v = xr[j];
+        if (v > m) { s = (m == -INFINITY) ? 0.f : s * expf(m - v); m = v; }
+        s += expf(v - m);
+      }
+      warp_online(m, s);
+      if (lane == 0) { sm_a[wid] = m; sm_b[wid] = s; }
+      __syncthreads();
+      if (wid == 0) {
+        m = lane < 8 ? sm_a[lane] : -INFINITY;
+        s = lane < 8 ? sm_b[lane] : 0.f;
+        warp_online(m, s);
+        if (lane == 0) { sm_a[0] = m; sm_b[0] = s; }
+      }
+      __syncthreads();
+      m = sm_a[0];
+      s = sm_b[0];
+      float* o = reinterpret_cast<float*>(out) + r * D;
+      if (KIND == ROW_LOGSOFTMAX) {
+        float lz = m + logf(s);
+        for (int64_t j = threadIdx.x; j < D; j += blockDim.x) o[j] = xr[j] - lz;
+      } else {
+        for (int64_t j = threadIdx.x; j < D; j += blockDim.x) o[j] = j < lim ? __fdiv_rn(expf(xr[j] - m), s) : 0.f;
+      }
+      __syncthreads();
+    }
+  }
+}
+
+// Long-row sum: partial sums of chunk-sized pieces into scratch.
+__global__ void __launch_bounds__(256) row_partial_kernel(const float* __restrict__ x, float* __restrict__ part,
+                                                          int64_t rows, int64_t D, int64_t nchunk, int64_t chunk) {
+  __shared__ float sm[8];
+  int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+  for (int64_t w = blockIdx.x; w < rows * nchunk; w += gridDim.x) {
+    int64_t r = w / nchunk, c = w % nchunk;
+    int64_t j0 = c * chunk, j1 = j0 + chunk < D ? j0 + chunk : D;
+    const float* xr = x + r * D;
+    float s = 0.f;
+    for (int64_t j = j0 + threadIdx.x; j < j1; j += blockDim.x) s += xr[j];
+    s = warp_sum(s);
+    if (lane == 0) sm[wid] = s;
+    __syncthreads();
+    if (wid == 0) {
+      s = lane < 8 ? sm[lane] : 0.f;
+      s = warp_sum(s);
+      if (lane == 0) part[w] = s;
+    }
+    __syncthreads();
+  }
+}
+
+__global__ void scale_div_kernel(float* v, int64_t n, float d) {
+  int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < n) v[i] = __fdiv_rn(v[i], d);
+}
+
+template <int KIND>
+static void dispatch_row(const float* x, void* out, int64_t rows, int64_t D, cudaStream_t s, const int* seed,
+                         uint32_t salt) {
+  int sms = device_sm_count();
+  if (D <= 2048) {
+    int64_t blocks = (rows * 32 + 255) / 256;
+    int64_t cap = (int64_t)sms * 16;
+    if (blocks > cap) blocks = cap;
+    if (blocks < 1) blocks = 1;
+    row_warp_kernel<KIND><<<(unsigned)blocks, 256, 0, s>>>(x, out, rows, D, seed, salt);
+  } else {
+    int64_t blocks = rows < (int64_t)sms * 8 ? rows : (int64_t)sms * 8;
+    if (blocks < 1) blocks = 1;
+    row_block_kernel<KIND><<<(unsigned)blocks, 256, 0, s>>>(x, out, rows, D, seed, salt);
+  }
+}
+
+// Number of chunk partials used for the long-row path; <= 1 means unused.
+static int64_t long_row_chunks(int64_t rows, int64_t D) {
+  int sms = device_sm_count();
+  if (rows >= sms || D < (1 << 15)) return 0;
+  int64_t want = ((int64_t)sms * 4 + rows - 1) / rows;
+  int64_t byD = D / 4096;
+  return want < byD ? want : byD;
+}
+
+size_t row_scratch_floats(int kind, int64_t rows, int64_t D) {
+  if (kind != ROW_SUM && kind != ROW_MEAN) return 0;
+  int64_t c = long_row_chunks(rows, D);
+  return c > 1 ? (size_t)(rows * c) : 0;
+}
+
+void launch_row(int kind, const float* x, void* out, int64_t rows, int64_t D, cudaStream_t s, const int* seed,
+                uint32_t salt, float* scratch, size_t scratch_floats) {
+  if (rows <= 0) return;
+  if (kind == ROW_SUM || kind == ROW_MEAN) {
+    int64_t c = long_row_chunks(rows, D);
+    if (c > 1 && scratch && scratch_floats >= (size_t)(rows * c)) {
+      int64_t chunk = (D + c - 1) / c;
+      row_partial_kernel<<<(unsigned)(rows * c), 256, 0, s>>>(x, scratch, rows, D, c, chunk);
+      dispatch_row<ROW_SUM>(scratch, out, rows, c, s, nullptr, 0);
+      // a mean divides the folded sum exactly by D, as the reference does
+      if (kind == ROW_MEAN)
+        scale_div_kernel<<<(unsigned)((rows + 255) / 256), 256, 0, s>>>(reinterpret_cast<float*>(out), rows,
+                                                                         (float)D);
+      return;
+    }
+  }
+  switch (kind) {
+    case ROW_SUM: dispatch_row<ROW_SUM>(x, out, rows, D, s, seed, salt); break;
+    case ROW_MEAN: dispatch_row<ROW_MEAN>(x, out, rows, D, s, seed, salt); break;
+    case ROW_ARGMAX: dispatch_row<ROW_ARGMAX>(x, out, rows, D, s, seed, salt); break;
+    case ROW_LOGSOFTMAX: dispatch_row<ROW_LOGSOFTMAX>(x, out, rows, D, s, seed, salt); break;
+    case ROW_SOFTMAX_CAUSAL: dispatch_row<ROW_SOFTMAX_CAUSAL>(x, out, rows, D, s, seed, salt); break;
+    case ROW_CATEGORICAL: dispatch_row<ROW_CATEGORICAL>(x, out, rows, D, s, seed, salt); break;
+  }
+}
+
+// -------------------------------------------------------------- column sum --
+static int64_t colsum_chunks(int64_t outer, int64_t inner) {
+  int sms = device_sm_count();
+  int64_t colblocks = (inner + 255) / 256;
+  int64_t want = ((int64_t)sms * 4 + colblocks - 1) / colblocks;
+  int64_t maxc = (outer + 63) / 64;  // at least 64 rows per chunk
+  int64_t c = want < maxc ? want : maxc;
+  return c < 1 ? 1 : c;
+}
+
+size_t colsum_scratch_floats(int64_t outer, int64_t inner) {
+  int64_t c = colsum_chunks(outer, inner);
+  return c > 1 ? (size_t)(c * inner) : 0;
+}
+
+__global__ void __launch_bounds__(256) colsum_partial_kernel(const float* __restrict__ x, float* __restrict__ part,
+                                                             int64_t outer, int64_t inner, int64_t rows_per) {
+  int64_t col = (int64_t)blockIdx.x * 256 + threadIdx.x;
+  int64_t c = blockIdx.y;
+  if (col >= inner) return;
+  int64_t r0 = c * rows_per, r1 = r0 + rows_per < outer ? r0 + rows_per : outer;
+  float s = 0.f;
+  for (int64_t r = r0; r < r1; ++r) s += x[r * inner + col];
+  part[c * inner + col] = s;
+}
+
+__global__ void __launch_bounds__(256) colsum_fold_kernel(const float* __restrict__ part, float* __restrict__ out,
+                                                          int64_t nchunk, int64_t inner) {
+  int64_t col = (int64_t)blockIdx.x * 256 + threadIdx.x;
+  if (col >= inner) return;
+  float s = 0.f;
+  for (int64_t c = 0; c < nchunk; ++c) s += part[c * inner + col];
+  out[col] = s;
+}
+
+void launch_colsum(const float* x, float* out, int64_t outer, int64_t inner, float* scratch, cudaStream_t s) {
+  if (inner <= 0) return;
+  int64_t c = colsum_chunks(outer, inner);
+  unsigned gx = (unsigned)((inner + 255) / 256);
+  if (c <= 1 || !scratch) {
+    colsum_partial_kernel<<<dim3(gx, 1), 256, 0, s>>>(x, out, outer, inner, outer);
+    return;
+  }
+  int64_t rows_per = (outer + c - 1) / c;
+  colsum_partial_kernel<<<dim3(gx, (unsigned)c), 256, 0, s>>>(x, scratch, outer, inner, rows_per);
+  colsum_fold_kernel<<<gx, 256, 0, s>>>(scratch, out, c, inner);
+}
+
+// ---------------------------------------------------- general sum to shape --
+struct SumGen {
+  int rank;
+  int64_t in_dims[8];
+  int64_t in_strides[8];
+  int64_t keep[8];
+  int64_t out_dims[8];
+  int64_t red_count;
+};
+
+__global__ void __launch_bounds__(256) sum_general_kernel(const float* __restrict__ x, float* __restrict__ out,
+                                                          const __grid_constant__ SumGen g, int64_t out_numel) {
+  __shared__ float sm[8];
+  int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+  for (int64_t o = blockIdx.x; o < out_numel; o += gridDim.x) {
+    int64_t base = 0, rem = o;
+    for (int d = g.rank - 1; d >= 0; --d) {
+      int64_t c = rem % g.out_dims[d];
+      rem /= g.out_dims[d];
+      if (g.keep[d]) base += c * g.in_strides[d];
+    }
+    float s = 0.f;
+    for (int64_t k = threadIdx.x; k < g.red_count; k += blockDim.x) {
+      int64_t off = base, rr = k;
+      for (int d = g.rank - 1; d >= 0; --d) {
+        if (g.keep[d]) continue;
+        int64_t c = rr % g.in_dims[d];
+        rr /= g.in_dims[d];
+        off += c * g.in_strides[d];
+      }
+      s += x[off];
+    }
+    s = warp_sum(s);
+    if (lane == 0) sm[wid] = s;
+    __syncthreads();
+    if (wid == 0) {
+      s = lane < 8 ? sm[lane] : 0.f;
+      s = warp_sum(s);
+      if (lane == 0) out[o] = s;
+    }
+    __syncthreads();
+  }
+}
+
+void launch_sum_general(const float* x, float* out, int rank, const int64_t* in_dims, const int64_t* keep,
+                        int64_t in_numel, int64_t out_numel, cudaStream_t s) {
+  SumGen g{};
+  g.rank = rank;
+  int64_t st = 1;
+  for (int d = rank - 1; d >= 0; --d) {
+    g.in_dims[d] = in_dims[d];
+    g.in_strides[d] = st;
+    st *= in_dims[d];
+    g.keep[d] = keep[d];
+    g.out_dims[d] = keep[d] ? in_dims[d] : 1;
+  }
+  g.red_count = out_numel > 0 ? in_numel / out_numel : 0;
+  int64_t cap = (int64_t)device_sm_count() * 16;
+  int64_t blocks = out_numel < cap ? out_numel : cap;
+  if (blocks < 1) return;
+  sum_general_kernel<<<(unsigned)blocks, 256, 0, s>>>(x, out, g, out_numel);
+}
+
+}  // namespace tg
