@@ -1,0 +1,101 @@
+/* tensorgrad_b200 — C ABI of the B200 execution backend (libtgcuda.so).
+ *
+ * This is the boundary the reference's worker would bind in place of its
+ * WebGPU runtime. Each entry point replaces one reference interface:
+ *
+ *   tg_ctx_create / tg_ctx_destroy   ensureDevice + the worker's device
+ *                                    ownership (src/worker.ts:58-82)
+ *   tg_nccl_unique_id                (new: data-parallel rendezvous token)
+ *   tg_graph_create                  createRuntime(plan, kernels, ...)
+ *                                    (src/runtime.ts:157-162) fed the traced
+ *                                    graph instead of WGSL kernels; the
+ *                                    worker's handleCreateRuntime /
+ *                                    handleCompileForward (src/worker.ts:86-170)
+ *   tg_graph_info                    CompiledRuntime.params/outputShape
+ *                                    (src/runtime.ts:123-137)
+ *   tg_upload_params                 uploadParams (src/runtime.ts:403-429)
+ *   tg_download_params               downloadParams (src/runtime.ts:431-449)
+ *   tg_step                          handleStep -> runtime.step
+ *                                    (src/worker.ts:216-240, src/runtime.ts:388-393)
+ *   tg_run                           handleRun -> runtime.run
+ *                                    (src/worker.ts:242-260, src/runtime.ts:395-400)
+ *   tg_set_inputs / tg_launch_step /
+ *   tg_read_loss / tg_stream         the three phases of dispatchUnsynchronized
+ *                                    (src/runtime.ts:314-386), split so a caller
+ *                                    can keep inputs resident and pipeline steps
+ *   tg_reset_optimizer               resetOptimizerState (src/runtime.ts:461-465,
+ *                                    src/worker.ts:295-302)
+ *   tg_set_lr                        handleSetLR (src/worker.ts:304-319)
+ *   tg_destroy_graph                 destroy + cascade (src/worker.ts:321-334)
+ *   tg_read_grad / tg_read_tensor    (new: inspection for parity tests)
+ *   tg_last_error_name/_message      the worker's serialized {name, message}
+ *                                    errors (src/worker-protocol.ts:118-177)
+ *
+ * All functions return 0 on success and a nonzero status otherwise; the
+ * thread-local error name/message describe the failure. Host pointers stay
+ * owned by the caller. A context is used from one thread at a time.
+ */
+#ifndef TENSORGRAD_B200_H
+#define TENSORGRAD_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct tg_ctx tg_ctx;
+
+enum {
+  TG_OK = 0,
+  TG_ERR = 1,       /* "Error" */
+  TG_ABORTED = 2,   /* "AbortError": graph destroyed or replaced mid-call */
+  TG_CUDA_ERR = 3,  /* "CudaError" */
+  TG_NCCL_ERR = 4,  /* "NcclError" */
+};
+
+int tg_nccl_unique_id(uint8_t out[128]);
+int tg_ctx_create(int device, int rank, int world, const uint8_t* nccl_id, tg_ctx** out);
+int tg_ctx_destroy(tg_ctx* ctx);
+
+/* program_json: {"graph": WireIR graph, "params", "inputs", "states",
+ * "paramGrads", "writebacks", "loss", "optimizer", "usesPrng", "optStart"}.
+ * parent_graph_id = -1 owns its params; otherwise params are shared with
+ * that graph (a forward sibling). */
+int tg_graph_create(tg_ctx* ctx, int graph_id, int parent_graph_id, const char* program_json, size_t len);
+/* Writes a JSON description into buf (params, launch count, device bytes). */
+int tg_graph_info(tg_ctx* ctx, int graph_id, char* buf, size_t cap, size_t* needed);
+int tg_upload_params(tg_ctx* ctx, int graph_id, int n, const char* const* names, const float* const* data,
+                     const size_t* numel);
+int tg_download_params(tg_ctx* ctx, int graph_id, int n, const char* const* names, float* const* out,
+                       const size_t* numel);
+/* One synchronous training step from host inputs: H2D, kernels, loss D2H. */
+int tg_step(tg_ctx* ctx, int graph_id, int n, const char* const* names, const void* const* data,
+            const size_t* bytes, float* loss_out, void* const* capture_out);
+/* One forward run: output (and captures) copied into caller buffers. */
+int tg_run(tg_ctx* ctx, int graph_id, int n, const char* const* names, const void* const* data,
+           const size_t* bytes, void* output_out, void* const* capture_out);
+/* Split step: copy inputs (device_src != 0: data are device pointers),
+ * enqueue a step without waiting, read the last loss (synchronizes). */
+int tg_set_inputs(tg_ctx* ctx, int graph_id, int n, const char* const* names, const void* const* data,
+                  const size_t* bytes, int device_src);
+int tg_launch_step(tg_ctx* ctx, int graph_id);
+int tg_read_loss(tg_ctx* ctx, int graph_id, float* loss_out);
+int tg_stream(tg_ctx* ctx, void** stream_out);
+int tg_reset_optimizer(tg_ctx* ctx, int graph_id);
+int tg_set_lr(tg_ctx* ctx, int graph_id, const char* lr_json, size_t len);
+int tg_destroy_graph(tg_ctx* ctx, int graph_id);
+int tg_read_grad(tg_ctx* ctx, int graph_id, const char* name, float* out);
+int tg_read_tensor(tg_ctx* ctx, int graph_id, int tensor_id, void* out);
+/* Newline-separated kind of every kernel launch in one step. */
+int tg_launch_list(tg_ctx* ctx, int graph_id, char* buf, size_t cap, size_t* needed);
+
+const char* tg_last_error_name(void);
+const char* tg_last_error_message(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* TENSORGRAD_B200_H */

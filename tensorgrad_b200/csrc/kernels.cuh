@@ -30,6 +30,7 @@ enum EwInMode : int {
   IN_PERIOD = 2,   // trailing-suffix broadcast: offset = i % period
   IN_ROWDIV = 3,   // leading-prefix broadcast ([..., 1] over [..., D]): offset = i / period
   IN_STRIDED = 4,  // general: offset = sum(coord_d * stride_d)
+  IN_ONEHOT = 5,   // virtual one-hot of int indices at ptr: (idx[i/period] == i%period) ? 1 : 0
 };
 
 struct EwInput {
@@ -122,13 +123,15 @@ void launch_randn(float* out, int64_t n, const int* seed, uint32_t salt_const, c
 // GEMM: C[b] (+)= alpha * A[b] @ B[b] (+ bias) with arbitrary strides.
 // ---------------------------------------------------------------------------
 struct GemmDesc {
-  int64_t M, N, K, batch;
+  int64_t M, N, K, batch;  // batch index z = i1 * batch2 + i2, i1 < batch / batch2
   const float* A; int64_t lda_m, lda_k, a_batch;  // A(m,k) = A[m*lda_m + k*lda_k]
   const float* B; int64_t ldb_k, ldb_n, b_batch;  // B(k,n) = B[k*ldb_k + n*ldb_n]
   float* C; int64_t ldc, c_batch;                 // C(m,n) = C[m*ldc + n]
   const float* bias;                              // optional [N], added in the epilogue
   float alpha;
   int accumulate;                                 // C += result
+  int64_t batch2;                                 // inner batch extent (1 = single batch dim)
+  int64_t a_batch2, b_batch2, c_batch2;           // strides of the inner batch index
 };
 void launch_gemm_simt(const GemmDesc& g, cudaStream_t s);
 // tcgen05/TMEM 3xTF32 GEMM; returns false when the shape/layout is not taken.

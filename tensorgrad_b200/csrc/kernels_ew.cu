@@ -86,7 +86,14 @@ __device__ __forceinline__ int64_t in_offset(const EwInput& in, const EwProgram&
 template <int V>
 __device__ __forceinline__ void load_input(const EwInput& in, const EwProgram& P, int64_t i, float (&o)[V]) {
   const float* base = reinterpret_cast<const float*>(in.ptr);
-  if (in.mode == IN_SCALAR) {
+  if (in.mode == IN_ONEHOT) {
+    const int* ix = reinterpret_cast<const int*>(in.ptr);
+#pragma unroll
+    for (int l = 0; l < V; ++l) {
+      int64_t e = i + l;
+      o[l] = (int64_t)__ldg(ix + e / in.period) == e % in.period ? 1.f : 0.f;
+    }
+  } else if (in.mode == IN_SCALAR) {
     float s = __ldg(base);
 #pragma unroll
     for (int l = 0; l < V; ++l) o[l] = s;

@@ -15,9 +15,10 @@ __global__ void __launch_bounds__(256) sgemm_kernel(const __grid_constant__ Gemm
   __shared__ float As[SG_BK][SG_BM + 4];
   __shared__ float Bs[SG_BK][SG_BN + 4];
   int64_t bz = blockIdx.z;
-  const float* A = g.A + bz * g.a_batch;
-  const float* B = g.B + bz * g.b_batch;
-  float* C = g.C + bz * g.c_batch;
+  int64_t i1 = bz / g.batch2, i2 = bz % g.batch2;
+  const float* A = g.A + i1 * g.a_batch + i2 * g.a_batch2;
+  const float* B = g.B + i1 * g.b_batch + i2 * g.b_batch2;
+  float* C = g.C + i1 * g.c_batch + i2 * g.c_batch2;
   int64_t m0 = (int64_t)blockIdx.y * SG_BM, n0 = (int64_t)blockIdx.x * SG_BN;
   int tid = threadIdx.x;
   int tm = (tid / 16) * 4, tn = (tid % 16) * 4;

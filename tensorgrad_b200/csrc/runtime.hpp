@@ -1,0 +1,190 @@
+// CUDA runtime behind the C ABI: loads a wire program (traced graph + plan
+// metadata), plans storage and a launch list for it, and executes training
+// steps / forward runs on one device stream, optionally inside a CUDA graph.
+//
+// This replaces the reference's WebGPU runtime (src/runtime.ts:157-499:
+// one GPUBuffer per BufferSpec, one compute pass per IR op, writeback copies
+// and a mapAsync per step) and its WGSL codegen (src/codegen.ts:48-56).
+#pragma once
+#include <cuda_runtime.h>
+#include <functional>
+#include <map>
+#include <memory>
+#include <stdexcept>
+#include <string>
+#include <vector>
+
+#include "json.hpp"
+#include "kernels.cuh"
+
+namespace tg {
+
+// Error with a reference-style name ("Error", "ShapeError", "CudaError", ...).
+struct TgError : std::runtime_error {
+  std::string name;
+  TgError(const std::string& n, const std::string& m) : std::runtime_error(m), name(n) {}
+};
+
+#define TG_CUDA(x)                                                                          \
+  do {                                                                                      \
+    cudaError_t e_ = (x);                                                                   \
+    if (e_ != cudaSuccess)                                                                  \
+      throw ::tg::TgError("CudaError", std::string(#x) + ": " + cudaGetErrorString(e_)); \
+  } while (0)
+
+struct TInfo {
+  std::vector<int64_t> shape;
+  int dtype = F32;
+  int64_t numel = 1;
+};
+
+struct Writeback {
+  int src;
+  std::string dest;
+  bool to_param;
+};
+
+// Parsed wire program. Field names mirror the reference's graph + BufferPlan
+// vocabulary (src/ir.ts:284-296, src/buffers.ts:61-80).
+struct Program {
+  tgjson::Value root;
+  std::vector<TInfo> T;
+  std::vector<const tgjson::Value*> ops;
+  std::vector<std::string> kind;
+  std::vector<int> out;
+  std::vector<std::vector<int>> op_inputs;
+  std::vector<int> producer;                 // tensor -> op index
+  std::vector<std::vector<int>> consumers;   // tensor -> op indices (with repeats removed)
+  std::vector<int> outputs;
+  std::vector<std::pair<std::string, int>> captures;
+  std::vector<std::pair<std::string, int>> params;  // graph order
+  std::map<std::string, int> inputs;                // tensor_input name -> tensor
+  struct State { std::string name; int tensor; double init; };
+  std::vector<State> states;
+  std::vector<std::pair<std::string, int>> grads;   // param name -> grad tensor
+  std::vector<Writeback> writebacks;
+  int loss = -1;
+  int opt_start = -1;  // index of the first optimizer-pass op (= number of ops before it)
+  const tgjson::Value* optimizer = nullptr;
+  bool uses_prng = false;
+
+  void parse(const char* json, size_t len);
+  const tgjson::Value& op(int i) const { return *ops[i]; }
+};
+
+enum ArenaKind : int {
+  AR_PARAM = 0, AR_GRAD, AR_M, AR_V, AR_STATE, AR_INPUT, AR_CONST, AR_PERSIST, AR_TEMP, AR_SCRATCH, AR_COUNT
+};
+
+// Where a tensor's elements live: a root tensor owns storage in an arena;
+// views (reshape, stop_gradient, same-shape sum_to_shape/broadcast_to,
+// leading-axis slices, permutes feeding GEMMs) point into their root with an
+// element offset and strides. A virtual one-hot has no storage at all.
+struct TView {
+  int root = -1;
+  int64_t off = 0;                 // element offset into the root's storage
+  std::vector<int64_t> strides;    // element strides per dim
+  bool contiguous = true;
+  bool onehot = false;             // virtual one-hot of `onehot_idx` with depth shape.back()
+  int onehot_idx = -1;
+};
+
+struct StorageLoc {
+  int arena = -1;
+  int64_t off = 0;  // bytes
+  int64_t bytes = 0;
+};
+
+class Context;
+
+class Graph {
+ public:
+  Graph(Context* ctx, int id, Graph* parent, const char* json, size_t len);
+  ~Graph();
+
+  int id;
+  Context* ctx;
+  Graph* parent;
+  Program P;
+
+  // host API
+  void upload_params(int n, const char* const* names, const float* const* data, const size_t* numel);
+  void download_params(int n, const char* const* names, float* const* out, const size_t* numel);
+  void set_inputs(int n, const char* const* names, const void* const* data, const size_t* bytes, bool device_src);
+  void launch_step();  // enqueue one step (scalars + kernels), no sync
+  void read_loss(float* out);
+  void read_output(void* out);
+  void read_captures(void* const* out);
+  void read_tensor(int t, void* out);
+  void read_grad(const std::string& name, float* out);
+  void reset_optimizer();
+  void set_lr(const char* lr_json, size_t len);
+  std::string info_json() const;
+  float* param_ptr(const std::string& name) const;
+  int64_t param_numel(const std::string& name) const;
+  int launches_per_step() const { return (int)launches_.size(); }
+  std::string launch_kinds() const;
+
+ private:
+  void plan();
+  void plan_views();
+  void plan_optimizer();
+  void plan_storage();
+  void emit_launches();
+  void run_launches(cudaStream_t s);
+  void init_constants();
+  void* ptr(int t) const;
+  const TView& view(int t) const { return views_[t]; }
+  bool is_contig(int t) const { return views_[t].contiguous && !views_[t].onehot; }
+  void host_scalars();
+
+  std::vector<TView> views_;
+  std::vector<int> action_;          // per op: planned action code
+  std::vector<StorageLoc> loc_;      // per root tensor
+  std::vector<int> op_done_;         // ops folded away
+  void* arena_[AR_COUNT] = {};
+  int64_t arena_bytes_[AR_COUNT] = {};
+  bool arena_owned_[AR_COUNT] = {};
+  int64_t scratch_bytes_ = 0;
+  std::map<std::string, int64_t> param_off_;   // byte offset in the param arena (or parent's)
+  std::map<std::string, int64_t> param_n_;
+  std::vector<std::pair<std::string, int>> layout_;  // flat arena order (name, numel)
+  int64_t flat_floats_ = 0;  // padded total floats of the flat arenas
+  int64_t n_decay_ = 0;
+  // fused optimizer
+  bool adam_fused_ = false, sgd_fused_ = false;
+  AdamFlatDesc adam_{};
+  SgdFlatDesc sgd_{};
+  int adam_lrt_ = -1, adam_shrink_ = -1, sgd_lr_ = -1;
+  // per-step host scalars
+  int64_t t_ = 0;
+  int64_t prng_ = 0;
+  std::vector<std::function<void(cudaStream_t)>> launches_;
+  std::vector<std::string> launch_kind_;
+  std::vector<std::function<void(cudaStream_t)>> post_;  // writebacks
+  cudaGraph_t cgraph_ = nullptr;
+  cudaGraphExec_t cexec_ = nullptr;
+  bool use_graph_ = true;
+  bool captured_ = false;
+  float* loss_host_ = nullptr;  // pinned
+  std::vector<std::pair<int, int64_t>> grad_copy_;  // (grad tensor, byte offset in the grad arena)
+  int64_t loss_avg_off_ = 0;
+  float scalar_host_[256] = {};  // pageable staging for per-step scalars
+  int scalar_n_ = 0;
+  tgjson::Value lr_override_;
+  bool has_lr_override_ = false;
+  friend class Context;
+};
+
+class Context {
+ public:
+  Context(int device, int rank, int world, const unsigned char* nccl_id);
+  ~Context();
+  int device, rank, world;
+  cudaStream_t stream = nullptr;
+  void* nccl = nullptr;  // ncclComm_t
+  std::map<int, std::unique_ptr<Graph>> graphs;
+  void allreduce_sum(float* buf, int64_t n, cudaStream_t s);
+};
+
+}  // namespace tg

@@ -1,0 +1,376 @@
+// Planner: wire program -> views, fused optimizer, storage arenas.
+//
+// Storage replaces the reference's planBuffers (src/buffers.ts:103-277):
+// instead of one buffer per param/grad/state plus pooled intermediates, the
+// planner lays params, their gradients and optimizer moments out as four
+// flat arenas with one identical layout (so one fused kernel updates every
+// parameter and one collective reduces every gradient), makes reshape-like
+// ops zero-copy views, and packs intermediates into one arena by liveness
+// (same best-fit idea and the same no-overlap invariant, checked below).
+#include <algorithm>
+#include <cmath>
+#include <cstdio>
+#include <set>
+
+#include "runtime.hpp"
+
+namespace tg {
+
+static int dtype_of(const std::string& s) {
+  if (s == "f32") return F32;
+  if (s == "i32") return I32;
+  return BOOL;
+}
+
+void Program::parse(const char* json, size_t len) {
+  root = tgjson::parse(json, len);
+  const auto& g = root["graph"];
+  const auto& ts = g["tensors"];
+  T.resize(ts.size());
+  for (size_t i = 0; i < ts.size(); ++i) {
+    for (auto& d : ts[i]["shape"].a) T[i].shape.push_back(d.i64());
+    T[i].dtype = dtype_of(ts[i]["dtype"].str());
+    T[i].numel = 1;
+    for (auto d : T[i].shape) T[i].numel *= d;
+  }
+  const auto& os = g["ops"];
+  producer.assign(T.size(), -1);
+  consumers.assign(T.size(), {});
+  for (size_t i = 0; i < os.size(); ++i) {
+    const auto& o = os[i];
+    ops.push_back(&o);
+    kind.push_back(o["kind"].str());
+    int ot = o["out"].i32();
+    out.push_back(ot);
+    producer[ot] = (int)i;
+    std::vector<int> in;
+    const std::string& k = kind.back();
+    auto add = [&](const char* f) { in.push_back(o[f].i32()); };
+    static const std::set<std::string> leaf = {"param_input", "tensor_input", "state_input", "arange",
+                                               "const_scalar", "const_fill"};
+    static const std::set<std::string> ab = {"add", "sub", "mul", "div", "min", "max", "less", "greater",
+                                             "matmul", "matmul_batched"};
+    if (leaf.count(k)) {
+    } else if (k == "randn") add("seed");
+    else if (ab.count(k)) { add("a"); add("b"); }
+    else if (k == "dropout" || k == "categorical_last") { add("a"); add("seed"); }
+    else if (k == "one_hot") add("indices");
+    else if (k == "where") { add("cond"); add("a"); add("b"); }
+    else if (k == "concat") { for (auto& x : o["inputs"].a) in.push_back(x.i32()); }
+    else if (k == "relu_grad") { add("x"); add("dy"); }
+    else if (k == "adam_update_m") { add("m"); add("g"); }
+    else if (k == "adam_update_v") { add("v"); add("g"); }
+    else if (k == "adam_update_p") {
+      add("p"); add("mNew"); add("vNew"); add("lrt");
+      if (!o["decayShrinkTensor"].is_null()) add("decayShrinkTensor");
+    }
+    else if (k == "conv2d") { add("input"); add("weight"); }
+    else if (k == "conv2d_input_grad") { add("weight"); add("dy"); }
+    else if (k == "conv2d_weight_grad") { add("input"); add("dy"); }
+    else if (k == "max_pool_2d") add("input");
+    else if (k == "max_pool_2d_grad") { add("input"); add("dy"); }
+    else add("a");
+    for (int t : in) {
+      auto& c = consumers[t];
+      if (c.empty() || c.back() != (int)i) c.push_back((int)i);
+    }
+    op_inputs.push_back(std::move(in));
+    if (k == "param_input") params.emplace_back(o["name"].str(), ot);
+    if (k == "tensor_input") inputs[o["name"].str()] = ot;
+  }
+  for (auto& x : g["outputs"].a) outputs.push_back(x.i32());
+  for (auto& kv : g["captures"].o) captures.emplace_back(kv.first, kv.second.i32());
+  if (auto* st = root.find("states"))
+    for (auto& kv : st->o) states.push_back({kv.first, kv.second["tensor"].i32(), kv.second["initValue"].num()});
+  if (auto* pg = root.find("paramGrads"))
+    for (auto& kv : pg->o) grads.emplace_back(kv.first, kv.second.i32());
+  if (auto* wb = root.find("writebacks"))
+    for (auto& w : wb->a) writebacks.push_back({w["source"].i32(), w["destName"].str(), w["destKind"].str() == "param"});
+  if (auto* l = root.find("loss")) if (!l->is_null()) loss = l->i32();
+  if (loss < 0 && !outputs.empty()) loss = outputs[0];
+  opt_start = (int)ops.size();
+  if (auto* s = root.find("optStart")) if (!s->is_null()) opt_start = s->i32();
+  if (auto* o = root.find("optimizer")) if (!o->is_null()) optimizer = o;
+  if (auto* u = root.find("usesPrng")) uses_prng = u->kind == tgjson::Value::Bool ? u->b : false;
+}
+
+static std::vector<int64_t> contig_strides(const std::vector<int64_t>& shape) {
+  std::vector<int64_t> s(shape.size(), 1);
+  for (int i = (int)shape.size() - 2; i >= 0; --i) s[i] = s[i + 1] * shape[i + 1];
+  return s;
+}
+
+// ---------------------------------------------------------------- views ----
+void Graph::plan_views() {
+  const int nT = (int)P.T.size(), nO = (int)P.ops.size();
+  views_.assign(nT, TView{});
+  for (int t = 0; t < nT; ++t) {
+    views_[t].root = t;
+    views_[t].strides = contig_strides(P.T[t].shape);
+  }
+  std::set<int> pinned;  // tensors that must own storage (observable results)
+  for (int t : P.outputs) pinned.insert(t);
+  for (auto& c : P.captures) pinned.insert(c.second);
+  for (auto& w : P.writebacks) pinned.insert(w.src);
+
+  auto is_gemm = [&](int op) { return P.kind[op] == "matmul" || P.kind[op] == "matmul_batched"; };
+
+  // Embedding patterns: matmul(one_hot(idx), table) -> row gather;
+  // matmul(permute(reshape(one_hot(idx))), dy) -> sorted segmented sum.
+  auto onehot_of = [&](int t) -> int {  // tensor id of the one_hot output feeding t, or -1
+    int p = P.producer[t];
+    if (p >= 0 && P.kind[p] == "one_hot" && P.T[t].dtype == F32) return t;
+    return -1;
+  };
+  std::vector<int> gather_op, embgrad_op;  // op indices
+  for (int i = 0; i < nO; ++i) {
+    if (P.kind[i] != "matmul") continue;
+    int a = P.op(i)["a"].i32(), b = P.op(i)["b"].i32();
+    if (onehot_of(a) >= 0 && P.T[b].shape.size() == 2 &&
+        P.op(P.producer[a])["depth"].i64() == P.T[b].shape[0]) {
+      action_[i] = 100;  // gather
+      continue;
+    }
+    int pa = P.producer[a];
+    if (pa >= 0 && P.kind[pa] == "permute") {
+      const auto& perm = P.op(pa)["perm"].a;
+      int r = P.op(pa)["a"].i32();
+      int pr = P.producer[r];
+      if (perm.size() == 2 && perm[0].i32() == 1 && pr >= 0 && P.kind[pr] == "reshape" &&
+          onehot_of(P.op(pr)["a"].i32()) >= 0 && P.T[r].shape.size() == 2 &&
+          P.consumers[a].size() == 1 && P.consumers[r].size() == 1 && !pinned.count(a) && !pinned.count(r)) {
+        action_[i] = 101;  // embedding grad
+        op_done_[pa] = 1;
+        op_done_[pr] = 1;
+      }
+    }
+  }
+  // One-hot stays virtual when every consumer reads it through a pattern
+  // above or as a full-shape elementwise input.
+  static const std::set<std::string> ew_kinds = {
+      "add", "sub", "mul", "div", "min", "max", "mul_scalar", "add_scalar", "sqrt", "rsqrt", "log", "exp",
+      "relu", "neg", "abs", "tanh", "sigmoid", "erf", "sin", "cos", "less", "greater", "where", "relu_grad",
+      "dropout", "where_causal", "broadcast_to"};
+  for (int i = 0; i < nO; ++i) {
+    if (P.kind[i] != "one_hot") continue;
+    int t = P.out[i];
+    bool ok = !pinned.count(t) && P.T[t].dtype == F32;
+    for (int c : P.consumers[t]) {
+      if (!ok) break;
+      if (action_[c] == 100) continue;
+      if (P.kind[c] == "reshape" && op_done_[c]) continue;
+      if (ew_kinds.count(P.kind[c]) && P.T[P.out[c]].shape == P.T[t].shape) continue;
+      ok = false;
+    }
+    if (ok) {
+      views_[t].onehot = true;
+      views_[t].onehot_idx = P.op(i)["indices"].i32();
+      op_done_[i] = 1;
+    }
+  }
+
+  // Zero-copy views, in op order so chains resolve.
+  for (int i = 0; i < nO; ++i) {
+    if (op_done_[i]) continue;
+    const std::string& k = P.kind[i];
+    int o = P.out[i];
+    if (pinned.count(o)) continue;
+    if (k == "reshape" || k == "stop_gradient" ||
+        ((k == "sum_to_shape" || k == "broadcast_to") &&
+         P.T[o].shape == P.T[P.op(i)["a"].i32()].shape)) {
+      int a = P.op(i)["a"].i32();
+      const TView& va = views_[a];
+      if (va.onehot || !va.contiguous) continue;
+      views_[o].root = va.root;
+      views_[o].off = va.off;
+      views_[o].contiguous = true;
+      op_done_[i] = 1;
+    } else if (k == "slice_range") {
+      int a = P.op(i)["a"].i32();
+      const TView& va = views_[a];
+      if (va.onehot || !va.contiguous) continue;
+      int ax = P.op(i)["axis"].i32();
+      bool lead = true;
+      for (int d = 0; d < ax; ++d) if (P.T[a].shape[d] != 1) lead = false;
+      if (!lead) continue;
+      views_[o].root = va.root;
+      views_[o].off = va.off + P.op(i)["start"].i64() * va.strides[ax];
+      views_[o].contiguous = true;
+      op_done_[i] = 1;
+    } else if (k == "permute") {
+      int a = P.op(i)["a"].i32();
+      const TView& va = views_[a];
+      if (va.onehot) continue;
+      bool all_gemm = !P.consumers[o].empty();
+      for (int c : P.consumers[o]) if (!is_gemm(c) || action_[c] >= 100) all_gemm = false;
+      if (!all_gemm) continue;
+      const auto& perm = P.op(i)["perm"].a;
+      views_[o].root = va.root;
+      views_[o].off = va.off;
+      views_[o].strides.clear();
+      for (auto& pv : perm) views_[o].strides.push_back(va.strides[pv.i32()]);
+      views_[o].contiguous = false;
+      op_done_[i] = 1;
+    }
+  }
+}
+
+// ------------------------------------------------------------ optimizer ----
+void Graph::plan_optimizer() {
+  if (parent) return;
+  std::map<std::string, int> param_t, grad_t, state_t;
+  for (auto& p : P.params) param_t[p.first] = p.second;
+  for (auto& g : P.grads) grad_t[g.first] = g.second;
+  for (auto& s : P.states) state_t[s.name] = s.tensor;
+  std::map<std::string, int> wb_src;
+  for (auto& w : P.writebacks) wb_src[(w.to_param ? "p:" : "s:") + w.dest] = w.src;
+  auto only_consumer = [&](int t, int op) {
+    return P.consumers[t].size() == 1 && P.consumers[t][0] == op;
+  };
+  const std::string okind = P.optimizer ? (*P.optimizer)["kind"].str() : std::string();
+  std::vector<std::pair<std::string, bool>> decayed;  // name, decayed
+  std::vector<int> fold;
+
+  if (okind == "adam") {
+    int lrt = -1, shrink_t = -1;
+    float shrink_lit = 1.f, b1 = 0, b2 = 0, eps = 0;
+    bool ok = !P.grads.empty();
+    for (auto& pg : P.grads) {
+      if (!ok) break;
+      const std::string& n = pg.first;
+      auto ip = wb_src.find("p:" + n), im = wb_src.find("s:adam_m_" + n), iv = wb_src.find("s:adam_v_" + n);
+      if (ip == wb_src.end() || im == wb_src.end() || iv == wb_src.end()) { ok = false; break; }
+      int op_p = P.producer[ip->second], op_m = P.producer[im->second], op_v = P.producer[iv->second];
+      if (P.kind[op_p] != "adam_update_p" || P.kind[op_m] != "adam_update_m" || P.kind[op_v] != "adam_update_v") {
+        ok = false; break;
+      }
+      const auto& OP = P.op(op_p); const auto& OM = P.op(op_m); const auto& OV = P.op(op_v);
+      int G = pg.second;
+      if (OP["p"].i32() != param_t[n] || OP["mNew"].i32() != P.out[op_m] || OP["vNew"].i32() != P.out[op_v] ||
+          OM["g"].i32() != G || OV["g"].i32() != G || OM["m"].i32() != state_t["adam_m_" + n] ||
+          OV["v"].i32() != state_t["adam_v_" + n] || !only_consumer(P.out[op_m], op_p) ||
+          !only_consumer(P.out[op_v], op_p) || !P.consumers[P.out[op_p]].empty()) {
+        ok = false; break;
+      }
+      if (lrt < 0) { lrt = OP["lrt"].i32(); b1 = (float)OM["beta1"].num(); b2 = (float)OV["beta2"].num();
+                     eps = (float)OP["eps"].num(); }
+      if (OP["lrt"].i32() != lrt || (float)OM["beta1"].num() != b1 || (float)OV["beta2"].num() != b2 ||
+          (float)OP["eps"].num() != eps) { ok = false; break; }
+      bool dec;
+      if (!OP["decayShrinkTensor"].is_null()) {
+        int st = OP["decayShrinkTensor"].i32();
+        if (shrink_t >= 0 && shrink_t != st) { ok = false; break; }
+        shrink_t = st; dec = true;
+      } else {
+        float lit = (float)OP["decayShrink"].num();
+        dec = lit != 1.0f;
+        if (dec) {
+          if (shrink_lit != 1.0f && shrink_lit != lit) { ok = false; break; }
+          shrink_lit = lit;
+        }
+      }
+      decayed.emplace_back(n, dec);
+      fold.push_back(op_p); fold.push_back(op_m); fold.push_back(op_v);
+    }
+    if (shrink_t >= 0 && shrink_lit != 1.0f) ok = false;
+    if (ok) {
+      adam_fused_ = true;
+      adam_lrt_ = lrt;
+      adam_shrink_ = shrink_t;
+      const double b1d = (*P.optimizer)["config"]["beta1"].num(), b2d = (*P.optimizer)["config"]["beta2"].num();
+      adam_.beta1 = (float)b1d; adam_.one_minus_beta1 = (float)(1.0 - b1d);
+      adam_.beta2 = (float)b2d; adam_.one_minus_beta2 = (float)(1.0 - b2d);
+      adam_.eps = eps;
+      adam_.shrink_lit = shrink_lit;
+    }
+  } else if (okind == "sgd") {
+    // p_new = sub(p, mul(broadcast_to(lr), upd)); upd = v_new | add(g_eff, mul_scalar(v_new, mu)) | g_eff
+    // v_new = add(mul_scalar(v, mu), g_eff); g_eff = G | add(G, mul_scalar(p, wd))
+    const auto& cfg = (*P.optimizer)["config"];
+    double mu = cfg["momentum"].num(), wd = cfg["weightDecay"].num();
+    bool nesterov = cfg["nesterov"].kind == tgjson::Value::Bool && cfg["nesterov"].b;
+    int lr_t = -1;
+    bool ok = !P.grads.empty();
+    for (auto& pg : P.grads) {
+      if (!ok) break;
+      const std::string& n = pg.first;
+      int G = pg.second, pt = param_t[n];
+      auto ip = wb_src.find("p:" + n);
+      if (ip == wb_src.end()) { ok = false; break; }
+      int o_sub = P.producer[ip->second];
+      if (P.kind[o_sub] != "sub" || P.op(o_sub)["a"].i32() != pt) { ok = false; break; }
+      int o_mul = P.producer[P.op(o_sub)["b"].i32()];
+      if (P.kind[o_mul] != "mul") { ok = false; break; }
+      int o_bc = P.producer[P.op(o_mul)["a"].i32()];
+      if (P.kind[o_bc] != "broadcast_to") { ok = false; break; }
+      int lr_here = P.op(o_bc)["a"].i32();
+      if (lr_t >= 0 && lr_here != lr_t) { ok = false; break; }
+      lr_t = lr_here;
+      int upd = P.op(o_mul)["b"].i32();
+      std::vector<int> f = {o_sub, o_mul, o_bc};
+      int g_eff = -1;
+      if (mu > 0) {
+        auto iv = wb_src.find("s:sgd_v_" + n);
+        if (iv == wb_src.end()) { ok = false; break; }
+        int vnew = iv->second;
+        int o_vadd = P.producer[vnew];
+        if (P.kind[o_vadd] != "add") { ok = false; break; }
+        int o_vms = P.producer[P.op(o_vadd)["a"].i32()];
+        if (P.kind[o_vms] != "mul_scalar" || P.op(o_vms)["a"].i32() != state_t["sgd_v_" + n]) { ok = false; break; }
+        g_eff = P.op(o_vadd)["b"].i32();
+        f.push_back(o_vadd); f.push_back(o_vms);
+        if (nesterov) {
+          int o_nadd = P.producer[upd];
+          if (P.kind[o_nadd] != "add" || P.op(o_nadd)["a"].i32() != g_eff) { ok = false; break; }
+          int o_nms = P.producer[P.op(o_nadd)["b"].i32()];
+          if (P.kind[o_nms] != "mul_scalar" || P.op(o_nms)["a"].i32() != vnew) { ok = false; break; }
+          f.push_back(o_nadd); f.push_back(o_nms);
+        } else if (upd != vnew) { ok = false; break; }
+      } else {
+        g_eff = upd;
+      }
+      bool dec = false;
+      if (g_eff != G) {
+        int o_gadd = P.producer[g_eff];
+        if (o_gadd < 0 || P.kind[o_gadd] != "add" || P.op(o_gadd)["a"].i32() != G) { ok = false; break; }
+        int o_gms = P.producer[P.op(o_gadd)["b"].i32()];
+        if (P.kind[o_gms] != "mul_scalar" || P.op(o_gms)["a"].i32() != pt) { ok = false; break; }
+        f.push_back(o_gadd); f.push_back(o_gms);
+        dec = true;
+      }
+      decayed.emplace_back(n, dec);
+      for (int x : f) fold.push_back(x);
+    }
+    if (ok) {
+      sgd_fused_ = true;
+      sgd_lr_ = lr_t;
+      sgd_.momentum = (float)mu;
+      sgd_.wd = (float)wd;
+      sgd_.nesterov = nesterov ? 1 : 0;
+    }
+  }
+  // Flat layout: decayed params first so one index split selects the shrink.
+  std::vector<std::string> order;
+  if (adam_fused_ || sgd_fused_) {
+    for (auto& d : decayed) if (d.second) order.push_back(d.first);
+    for (auto& d : decayed) if (!d.second) order.push_back(d.first);
+    for (int x : fold) op_done_[x] = 1;
+  }
+  for (auto& p : P.params)
+    if (std::find(order.begin(), order.end(), p.first) == order.end()) order.push_back(p.first);
+  int64_t off = 0;
+  n_decay_ = 0;
+  for (auto& n : order) {
+    int64_t numel = P.T[param_t[n]].numel;
+    bool dec = false;
+    for (auto& d : decayed) if (d.first == n) dec = d.second;
+    layout_.emplace_back(n, (int)numel);
+    param_off_[n] = off * 4;
+    param_n_[n] = numel;
+    off += (numel + 63) / 64 * 64;
+    if (dec) n_decay_ = off;
+  }
+  flat_floats_ = off;
+}
+
+}  // namespace tg
