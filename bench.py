@@ -1,0 +1,279 @@
+"""Benchmark: train samples/sec for the GPT d384 L6 T256 config (config 4).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--config c4]
+
+One step = forward + backward + AdamW update of GPT(V=65, T=256, d=384,
+L=6, H=6, dropout 0.2) on 64 sequences per GPU (weak scaling: global batch
+64*N, data-parallel gradient allreduce over NCCL). Prints one JSON line.
+
+* value: samples/s with inputs resident on the device, K steps timed with CUDA
+  events on the backend's stream, max over ranks.
+* e2e: samples/s through the public step call (host inputs -> H2D each step,
+  loss D2H each step), same K.
+* roofline: the dominant kernel class of one step, measured live with events
+  around every launch (tg_profile_step).
+* cpu_baseline: the CPU oracle (numpy restatement of the reference's CPU
+  evaluator, f64 accumulate) on a bounded sample, rank 0 only.
+* --impl reference: times that CPU path alone on the same config and prints
+  the reference line (the reference is a browser WebGPU library; its own CPU
+  evaluator is the only implementation runnable here).
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+from tensorgrad_b200 import configs as CF  # noqa: E402
+
+METRIC = "train samples/sec (GPT d384 L6 T256, config 4)"
+UNIT = "samples/s"
+
+
+def peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        d = json.load(open(p))
+        return d["hbm_gbs"], d["bf16_tflops"], d.get("bf16_tflops_sustained", d["bf16_tflops"]), "measured"
+    return 6650.0, 1590.0, 1400.0, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clocks/throttle reasons sampled during the timed region."""
+
+    def __init__(self, device: int):
+        self.device = device
+        self.samples = []
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.device), "--query-gpu=clocks.sm,clocks.max.sm,power.draw,"
+                 "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+                 "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except Exception:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            parts = [x.strip() for x in line.split(",")]
+            if len(parts) >= 7:
+                self.samples.append(parts)
+
+    def __exit__(self, *a):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+
+    def summary(self):
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        sm = [float(s[0]) for s in self.samples if s[0].replace(".", "").isdigit()]
+        mx = [float(s[1]) for s in self.samples if s[1].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for s in self.samples for i in range(4) if s[3 + i].lower() == "active"})
+        return {"sm_mhz": float(np.median(sm)) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(self.samples)}
+
+
+def dist_env():
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return rank, world, local
+
+
+def gemm_flops_of(program, kinds):
+    """Algorithmic FLOPs of the GEMM launches, in launch order."""
+    g = program["graph"]
+    T = g["tensors"]
+    fl = []
+    for op in g["ops"]:
+        if op["kind"] in ("matmul", "matmul_batched"):
+            a, b, o = T[op["a"]]["shape"], T[op["b"]]["shape"], T[op["out"]]["shape"]
+            K = a[-1]
+            n = 1
+            for d in o:
+                n *= d
+            fl.append(2.0 * n * K)
+    return fl
+
+
+def cpu_baseline(w, sample_batch: int, threads: int):
+    """Times one oracle training step on `sample_batch` sequences."""
+    from oracle.driver import OracleTrainer
+    from tensorgrad_b200.compile import build_training_ir, initial_params
+    os.environ.setdefault("OMP_NUM_THREADS", str(threads))
+    ir = build_training_ir(w.make_model(), w.loss, w.inputs(sample_batch), w.optimizer)
+    init = initial_params(ir.graph, ir.materialized.initFns, CF.PARAM_SEED)
+    orc = OracleTrainer(ir.program, init)
+    data = w.data(sample_batch)
+    t0 = time.perf_counter()
+    orc.step(data)
+    dt = time.perf_counter() - t0
+    return sample_batch / dt, dt
+
+
+def run_reference(args, w):
+    rank, world, _ = dist_env()
+    if rank != 0:
+        return
+    threads = os.cpu_count() or 1
+    sample = 2
+    vals = []
+    for _ in range(max(1, args.steps)):
+        v, dt = cpu_baseline(w, sample, threads)
+        vals.append(v)
+    v = float(np.median(vals))
+    line = {"impl": "reference", "metric": METRIC, "value": v, "unit": UNIT, "n_gpus": args.gpus,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000.0 * sample / v,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic (mulberry32 seed 1234 tokens)",
+            "config": {"workload": w.name, "global_batch": sample, "seq_len": w.extra.get("T"),
+                       "parallelism": "cpu"},
+            "cpu_baseline": {"value": v, "unit": UNIT, "cores": threads, "kind": "port",
+                             "sample": f"one training step at batch {sample} (T=256, full model) per timed step; "
+                                       "numpy restatement of the reference CPU evaluator"},
+            "e2e": {"value": v, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=30)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="ours")
+    ap.add_argument("--config", default="c4")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    w = CF.workload(args.config)
+    if args.impl == "reference":
+        return run_reference(args, w)
+
+    import torch
+    from tensorgrad_b200 import backend as BK
+    from tensorgrad_b200.compile import build_training_ir, initial_params
+
+    rank, world, local = dist_env()
+    torch.cuda.set_device(local)
+    nccl_id = None
+    if world > 1:
+        import torch.distributed as dist
+        dist.init_process_group("gloo")
+        obj = [BK.nccl_unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(obj, src=0)
+        nccl_id = obj[0]
+    ctx = BK.Context(local, rank, world, nccl_id)
+    per_rank = w.global_batch
+    gb = per_rank * world
+    ir = build_training_ir(w.make_model(), w.loss, w.inputs(per_rank), w.optimizer)
+    init = initial_params(ir.graph, ir.materialized.initFns, CF.PARAM_SEED)
+    dg = BK.DeviceGraph(ctx, ir.program)
+    dg.upload_params(init)
+    data = CF.shard(w.data(gb), rank, world)
+    in_bytes = sum(v.nbytes for v in data.values())
+
+    stream = torch.cuda.ExternalStream(ctx.stream())
+
+    def barrier():
+        if world > 1:
+            import torch.distributed as dist
+            dist.barrier()
+
+    # warm-up (captures the CUDA graph on the first step)
+    dg.set_inputs(data)
+    for _ in range(args.warmup):
+        dg.launch_step()
+    dg.read_loss()
+
+    # value: resident inputs, device-timed
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier()
+    torch.cuda.synchronize()
+    with ClockSampler(local) as clk:
+        e0.record(stream)
+        for _ in range(args.steps):
+            dg.launch_step()
+        e1.record(stream)
+        loss = dg.read_loss()
+        torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1)
+    barrier()
+    # e2e: public step call with host buffers
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        dg.step(data)
+    e2e_ms = (time.perf_counter() - t0) * 1000.0
+    ms_t = torch.tensor([ms, e2e_ms], dtype=torch.float64)
+    if world > 1:
+        import torch.distributed as dist
+        dist.all_reduce(ms_t, op=dist.ReduceOp.MAX)
+    ms, e2e_ms = float(ms_t[0]), float(ms_t[1])
+
+    # per-launch profile (outside the timed region)
+    kinds = dg.launch_list()
+    prof = dg.profile_step()
+    by_kind = {}
+    for k, t in zip(kinds, prof):
+        by_kind[k] = by_kind.get(k, 0.0) + t
+    hbm, bf16, bf16s, src = peaks()
+    gemm_ms = sum(t for k, t in zip(kinds, prof) if k in ("matmul", "matmul_batched"))
+    gemm_fl = sum(gemm_flops_of(ir.program, kinds))
+    dom = max(by_kind.items(), key=lambda kv: kv[1])[0]
+    roof = {"bound": "tensor", "kernel": "matmul+matmul_batched (all GEMM launches of one step)",
+            "achieved": gemm_fl / (gemm_ms * 1e-3) / 1e12 if gemm_ms > 0 else None, "peak": bf16,
+            "unit": "TFLOP/s", "peak_source": f"{src} bf16 dense (MEASURED_PEAKS.json)", "traffic": None}
+    roof["frac"] = roof["achieved"] / bf16 if roof["achieved"] else None
+    roof["frac_of_3xtf32_effective"] = roof["achieved"] / (bf16 / 6.0) if roof["achieved"] else None
+    roof["dominant_kind"] = dom
+    roof["step_share"] = {k: round(v / sum(prof), 4) for k, v in sorted(by_kind.items(), key=lambda kv: -kv[1])[:8]}
+
+    value = args.steps * gb / (ms * 1e-3)
+    e2e = args.steps * gb / (e2e_ms * 1e-3)
+    line = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic (mulberry32 seed 1234 tokens, random-init params seed 42)",
+            "config": {"workload": w.name, "model": "GPT V65 T256 d384 L6 H6 dropout0.2", "global_batch": gb,
+                       "seq_len": 256, "parallelism": f"dp{world}",
+                       "l2": "inputs and activations exceed L2 (126 MB) every step"},
+            "e2e": {"value": e2e, "unit": UNIT, "h2d_bytes_per_step": in_bytes, "d2h_bytes_per_step": 4},
+            "gpu_launches": len(kinds) * args.steps, "roofline": roof, "clocks": clk.summary(),
+            "loss": loss, "tokens_per_s": value * 256,
+            "tflops_algorithmic": w.flops_per_sample * value / 1e12}
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        v, dt = cpu_baseline(w, 2, os.cpu_count() or 1)
+        line["cpu_baseline"] = {"value": v, "unit": UNIT, "cores": os.cpu_count() or 1, "kind": "port",
+                                "sample": f"one oracle training step at batch 2 ({dt:.1f} s); numpy f64 "
+                                          "restatement of the reference CPU evaluator"}
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    dg.destroy()
+    ctx.close()
+    if world > 1:
+        import torch.distributed as dist
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

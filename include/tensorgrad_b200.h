@@ -28,6 +28,9 @@
  *   tg_set_lr                        handleSetLR (src/worker.ts:304-319)
  *   tg_destroy_graph                 destroy + cascade (src/worker.ts:321-334)
  *   tg_read_grad / tg_read_tensor    (new: inspection for parity tests)
+ *   tg_launch_list / tg_profile_step (new: per-kernel launch list and timing;
+ *                                    the reference labels its compute passes
+ *                                    for browser profilers, src/runtime.ts:340)
  *   tg_last_error_name/_message      the worker's serialized {name, message}
  *                                    errors (src/worker-protocol.ts:118-177)
  *
@@ -90,6 +93,10 @@ int tg_read_grad(tg_ctx* ctx, int graph_id, const char* name, float* out);
 int tg_read_tensor(tg_ctx* ctx, int graph_id, int tensor_id, void* out);
 /* Newline-separated kind of every kernel launch in one step. */
 int tg_launch_list(tg_ctx* ctx, int graph_id, char* buf, size_t cap, size_t* needed);
+
+/* Runs one step launch by launch with CUDA events around each launch and
+ * writes per-launch milliseconds (in tg_launch_list order). */
+int tg_profile_step(tg_ctx* ctx, int graph_id, float* ms_out, int cap, int* n_out);
 
 const char* tg_last_error_name(void);
 const char* tg_last_error_message(void);

@@ -21,7 +21,7 @@ EXPORTED = [
     "tg_nccl_unique_id", "tg_ctx_create", "tg_ctx_destroy", "tg_graph_create", "tg_graph_info",
     "tg_upload_params", "tg_download_params", "tg_step", "tg_run", "tg_set_inputs", "tg_launch_step",
     "tg_read_loss", "tg_stream", "tg_reset_optimizer", "tg_set_lr", "tg_destroy_graph", "tg_read_grad",
-    "tg_read_tensor", "tg_launch_list", "tg_last_error_name", "tg_last_error_message",
+    "tg_read_tensor", "tg_launch_list", "tg_profile_step", "tg_last_error_name", "tg_last_error_message",
 ]
 
 
@@ -74,6 +74,7 @@ def load(path: str = LIB_PATH):
         "tg_destroy_graph": [vp, ip],
         "tg_read_grad": [vp, ip, C.c_char_p, vp],
         "tg_read_tensor": [vp, ip, ip, vp],
+        "tg_profile_step": [vp, ip, C.POINTER(C.c_float), ip, C.POINTER(C.c_int)],
     }
     for name, args in sig.items():
         f = getattr(lib, name)
@@ -162,6 +163,13 @@ class DeviceGraph:
         buf = C.create_string_buffer(need.value + 1)
         _check(self.lib.tg_launch_list(self.ctx.h, self.id, buf, len(buf), C.byref(need)))
         return [s for s in buf.value.decode().split("\n") if s]
+
+    def profile_step(self) -> List[float]:
+        n = C.c_int()
+        cap = 1 << 16
+        buf = (C.c_float * cap)()
+        _check(self.lib.tg_profile_step(self.ctx.h, self.id, buf, cap, C.byref(n)))
+        return [buf[i] for i in range(min(n.value, cap))]
 
     # -- params -----------------------------------------------------------
     def upload_params(self, params: Dict[str, np.ndarray]) -> None:

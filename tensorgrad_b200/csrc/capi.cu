@@ -191,6 +191,15 @@ int tg_read_tensor(tg_ctx* ctx, int graph_id, int tensor_id, void* out) {
   return guarded([&] { get_graph(ctx, graph_id)->read_tensor(tensor_id, out); });
 }
 
+int tg_profile_step(tg_ctx* ctx, int graph_id, float* ms_out, int cap, int* n_out) {
+  return guarded([&] {
+    std::vector<float> ms;
+    get_graph(ctx, graph_id)->profile_step(ms);
+    if (n_out) *n_out = (int)ms.size();
+    for (int i = 0; i < cap && i < (int)ms.size(); ++i) ms_out[i] = ms[i];
+  });
+}
+
 const char* tg_last_error_name(void) { return g_err_name.c_str(); }
 const char* tg_last_error_message(void) { return g_err_msg.c_str(); }
 

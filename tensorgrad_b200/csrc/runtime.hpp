@@ -124,6 +124,9 @@ class Graph {
   int64_t param_numel(const std::string& name) const;
   int launches_per_step() const { return (int)launches_.size(); }
   std::string launch_kinds() const;
+  // Runs one step launch by launch (no CUDA graph) with events around each
+  // launch; fills per-launch milliseconds.
+  void profile_step(std::vector<float>& ms);
 
  private:
   void plan();

@@ -1046,6 +1046,23 @@ void Graph::set_lr(const char* lr_json, size_t len) {
   has_lr_override_ = true;
 }
 
+void Graph::profile_step(std::vector<float>& ms) {
+  cudaStream_t s = ctx->stream;
+  host_scalars();
+  std::vector<cudaEvent_t> ev(launches_.size() + 1);
+  for (auto& x : ev) TG_CUDA(cudaEventCreate(&x));
+  TG_CUDA(cudaEventRecord(ev[0], s));
+  for (size_t i = 0; i < launches_.size(); ++i) {
+    launches_[i](s);
+    TG_CUDA(cudaEventRecord(ev[i + 1], s));
+  }
+  TG_CUDA(cudaStreamSynchronize(s));
+  TG_CUDA(cudaGetLastError());
+  ms.assign(launches_.size(), 0.f);
+  for (size_t i = 0; i < launches_.size(); ++i) TG_CUDA(cudaEventElapsedTime(&ms[i], ev[i], ev[i + 1]));
+  for (auto& x : ev) cudaEventDestroy(x);
+}
+
 std::string Graph::launch_kinds() const {
   std::string s;
   for (auto& k : launch_kind_) { s += k; s += '\n'; }

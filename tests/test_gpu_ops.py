@@ -1,0 +1,189 @@
+"""Per-op parity: each IR op kind runs through the C ABI on the GPU and is
+compared with the oracle on the same seeded inputs. Tolerance for f32:
+|gpu - ref| <= 1e-4 * max(|ref|, 1e-3 * max|ref|) per element (plus a 1e-7
+absolute floor for exact zeros); i32 outputs and dropout masks must match
+bit for bit."""
+import numpy as np
+import pytest
+
+import tensorgrad_b200 as tg
+from oracle.evaluator import eval_graph
+from tensorgrad_b200 import backend as BK
+from tensorgrad_b200.compile import _program
+from tensorgrad_b200.ir import graph_to_wire
+from tensorgrad_b200.module import Mulberry32
+from tensorgrad_b200.trace import tensor_input, trace_fn
+
+pytestmark = pytest.mark.gpu
+
+RTOL = 1e-4
+
+
+def close(gpu, ref, rtol=RTOL, floor=1e-7):
+    gpu = np.asarray(gpu, np.float64)
+    ref = np.asarray(ref, np.float64)
+    scale = np.maximum(np.abs(ref), 1e-3 * max(np.abs(ref).max(), 1e-30))
+    err = np.abs(gpu - ref)
+    ok = err <= rtol * scale + floor
+    i = int(np.argmax(err / (scale + 1e-30)))
+    assert ok.all(), f"max rel err {np.max(err / (scale + 1e-30)):.3e} at {i}: gpu={gpu.reshape(-1)[i]} ref={ref.reshape(-1)[i]}"
+
+
+def rnd(shape, seed=1, lo=-1.0, hi=1.0):
+    n = int(np.prod(shape)) if len(shape) else 1
+    return (lo + (hi - lo) * Mulberry32(seed).take(n)).astype(np.float32).reshape(shape)
+
+
+def run(ctx, build, inputs, exact=False, rtol=RTOL):
+    g = trace_fn(build)
+    prog = _program(g, {}, [], g.outputs[0], None, len(g.ops))
+    prog["usesPrng"] = False  # the test passes __prngSeed itself
+    dg = BK.DeviceGraph(ctx, prog)
+    try:
+        out, _ = dg.run(inputs)
+    finally:
+        dg.destroy()
+    ref = eval_graph(graph_to_wire(g), inputs)[g.outputs[0]]
+    if exact:
+        assert np.array_equal(out, ref.reshape(out.shape))
+    else:
+        close(out, ref.reshape(out.shape), rtol)
+    return out
+
+
+T = tensor_input
+
+
+def test_binops_broadcast(ctx):
+    ins = {"a": rnd([4, 5, 8], 1), "b": rnd([8], 2), "c": rnd([4, 5, 1], 3), "d": rnd([5, 1], 4)}
+
+    def build():
+        A, B, C, D = T("a", [4, 5, 8]), T("b", [8]), T("c", [4, 5, 1]), T("d", [5, 1])
+        x = tg.sub(tg.mul(tg.add(A, B), C), D)
+        x = tg.div(x, tg.add(tg.abs(C), 0.5))
+        return tg.max(tg.min(x, 0.7), -0.6)
+    run(ctx, build, ins)
+
+
+@pytest.mark.parametrize("name", ["exp", "tanh", "sigmoid", "erf", "sin", "cos", "relu", "neg", "abs", "gelu"])
+def test_unary(ctx, name):
+    fn = getattr(tg, name)
+    run(ctx, lambda: fn(T("a", [3, 1000])), {"a": rnd([3, 1000], 5, -3, 3)})
+
+
+@pytest.mark.parametrize("name", ["sqrt", "rsqrt", "log"])
+def test_unary_positive(ctx, name):
+    fn = getattr(tg, name)
+    run(ctx, lambda: fn(T("a", [3, 1000])), {"a": rnd([3, 1000], 6, 0.1, 4)})
+
+
+def test_compare_where(ctx):
+    ins = {"a": rnd([6, 7], 7)}
+    run(ctx, lambda: tg.leakyRelu(T("a", [6, 7]), 0.3), ins)
+    run(ctx, lambda: tg.leakyRelu(T("a", [6, 7]), 2.0), ins)
+
+
+def test_where_with_broadcast_branches(ctx):
+    ins = {"a": rnd([6, 7], 7), "b": rnd([7], 8)}
+
+    def build():
+        a, b = T("a", [6, 7]), T("b", [7])
+        return tg.where(tg.less(a, b), tg.mul(a, 3.0), tg.neg(b))
+    run(ctx, build, ins)
+
+
+def test_reductions(ctx):
+    a = rnd([33, 257], 9)
+    run(ctx, lambda: tg.sum(T("a", [33, 257]), -1), {"a": a})
+    run(ctx, lambda: tg.mean(T("a", [33, 257]), -1, keepDims=True), {"a": a})
+    run(ctx, lambda: tg.mean(T("a", [33, 257])), {"a": a})
+    run(ctx, lambda: tg.sum(T("a", [33, 257]), 0), {"a": a})
+
+
+def test_long_row_sum(ctx):
+    a = rnd([1, 1 << 20], 10)
+    run(ctx, lambda: tg.mean(T("a", [1, 1 << 20])), {"a": a})
+
+
+def test_argmax_exact_with_ties(ctx):
+    a = np.floor(rnd([64, 300], 11, 0, 4)).astype(np.float32)  # many ties: first max must win
+    run(ctx, lambda: tg.argmax(T("a", [64, 300]), -1), {"a": a}, exact=True)
+    run(ctx, lambda: tg.argmin(T("a", [64, 300]), -1), {"a": a}, exact=True)
+    big = np.floor(rnd([3, 5000], 12, 0, 3)).astype(np.float32)
+    run(ctx, lambda: tg.argmax(T("a", [3, 5000]), -1), {"a": big}, exact=True)
+
+
+def test_softmaxes(ctx):
+    a = rnd([2, 3, 40, 40], 13, -4, 4)
+    run(ctx, lambda: tg.softmaxCausal(T("a", [2, 3, 40, 40])), {"a": a})
+    run(ctx, lambda: tg.logSoftmax(T("a", [2, 3, 40, 40])), {"a": a})
+    run(ctx, lambda: tg.softmax(T("a", [2, 3, 40, 40]), 2), {"a": a})
+    w = rnd([4, 3000], 14, -4, 4)
+    run(ctx, lambda: tg.logSoftmax(T("a", [4, 3000])), {"a": w})
+    s = rnd([2, 2100, 2100], 15, -2, 2)
+    run(ctx, lambda: tg.softmaxCausal(T("a", [2, 2100, 2100])), {"a": s})
+
+
+def test_where_causal_and_dropout_exact(ctx):
+    a = rnd([2, 16, 16], 16)
+    run(ctx, lambda: tg.whereCausal(T("a", [2, 16, 16]), -1e9), {"a": a}, exact=True)
+    x = rnd([8, 1024], 17)
+    seed = np.array(42, np.int32)
+    run(ctx, lambda: tg.dropout(tg.dropout(T("x", [8, 1024]), 0.2), 0.5), {"x": x, "__prngSeed": seed}, exact=True)
+
+
+def test_layout_ops(ctx):
+    a = rnd([3, 4, 5, 6], 18)
+    run(ctx, lambda: tg.permute(T("a", [3, 4, 5, 6]), [2, 0, 3, 1]), {"a": a}, exact=True)
+    run(ctx, lambda: tg.narrow(T("a", [3, 4, 5, 6]), 2, 1, 3), {"a": a}, exact=True)
+    run(ctx, lambda: tg.narrow(T("a", [3, 4, 5, 6]), 0, 1, 2), {"a": a}, exact=True)
+    b = rnd([3, 4, 2, 6], 19)
+    run(ctx, lambda: tg.concat([T("a", [3, 4, 5, 6]), T("b", [3, 4, 2, 6])], 2), {"a": a, "b": b}, exact=True)
+    run(ctx, lambda: tg.scatterAxis(T("b", [3, 4, 2, 6]), [3, 4, 5, 6], 2, 1, 3), {"b": b}, exact=True)
+    run(ctx, lambda: tg.broadcastTo(T("c", [1, 6]), [3, 4, 5, 6]), {"c": rnd([1, 6], 20)}, exact=True)
+    run(ctx, lambda: tg.sumToShape(T("a", [3, 4, 5, 6]), [4, 1, 6]), {"a": a})
+
+
+@pytest.mark.parametrize("M,K,N", [(1, 1, 1), (37, 29, 53), (256, 384, 200), (130, 1, 70)])
+def test_matmul_2d(ctx, M, K, N):
+    run(ctx, lambda: tg.matmul(T("a", [M, K]), T("b", [K, N])), {"a": rnd([M, K], 21), "b": rnd([K, N], 22)})
+
+
+def test_matmul_transposed_views_and_batched(ctx):
+    a, b = rnd([2, 3, 17, 24], 23), rnd([2, 3, 19, 24], 24)
+    run(ctx, lambda: tg.matmul(T("a", [2, 3, 17, 24]), tg.swapAxes(T("b", [2, 3, 19, 24]), -1, -2)),
+        {"a": a, "b": b})
+    x = rnd([2, 17, 3, 8], 25)
+
+    def heads():
+        h = tg.swapAxes(T("x", [2, 17, 3, 8]), 1, 2)          # [2,3,17,8] strided view
+        s = tg.matmul(h, tg.swapAxes(h, -1, -2))              # [2,3,17,17]
+        return tg.matmul(s, h)
+    run(ctx, heads, {"x": x})
+    w = rnd([24, 10], 26)
+    run(ctx, lambda: tg.matmul(tg.swapAxes(T("w", [24, 10]), 0, 1), T("v", [24, 7])), {"w": w, "v": rnd([24, 7], 27)})
+
+
+def test_embedding_gather_and_onehot(ctx):
+    idx = np.floor(rnd([5, 7], 28, 0, 11)).astype(np.int32)
+    tab = rnd([11, 12], 29)
+    run(ctx, lambda: tg.embedding(T("t", [11, 12]), T("i", [5, 7], "i32")), {"t": tab, "i": idx}, exact=True)
+    run(ctx, lambda: tg.oneHot(T("i", [5, 7], "i32"), 11), {"i": idx}, exact=True)
+
+
+def test_conv_and_pool(ctx):
+    x = rnd([2, 4, 9, 9], 30)
+    w = rnd([6, 2, 3, 3], 31)
+    run(ctx, lambda: tg.conv2d(T("x", [2, 4, 9, 9]), T("w", [6, 2, 3, 3]), stride=2, padding=1, groups=2),
+        {"x": x, "w": w})
+    q = np.floor(rnd([2, 3, 8, 8], 32, 0, 3)).astype(np.float32)
+    run(ctx, lambda: tg.maxPool2d(T("x", [2, 3, 8, 8]), 2), {"x": q}, exact=True)
+    run(ctx, lambda: tg.maxPool2d(T("x", [2, 3, 8, 8]), 3, stride=2, padding=1), {"x": q}, exact=True)
+
+
+def test_randn_and_categorical(ctx):
+    seed = np.array(5, np.int32)
+    run(ctx, lambda: tg.add(tg.randn([4, 1000]), T("z", [1000])), {"z": np.zeros(1000, np.float32),
+                                                                   "__prngSeed": seed}, rtol=1e-3)
+    logits = rnd([16, 50], 33, -2, 2)
+    run(ctx, lambda: tg.categorical(T("l", [16, 50])), {"l": logits, "__prngSeed": seed}, exact=True)
