@@ -243,7 +243,7 @@ def eval_op(op: dict, vals: Dict[int, np.ndarray], inputs: Dict[str, np.ndarray]
         h2 = pcg_hash(h1)
         u1 = np.maximum(np.float32(1e-10), h1.astype(np.float32) / np.float32(4294967296.0)).astype(F64)
         u2 = (h2.astype(np.float32) / np.float32(4294967296.0)).astype(F64)
-        return _store(np.sqrt(-2.0 * np.log(u1)) * np.cos(2 * np.pi * u2), shape, dt)
+        return _store((np.sqrt(-2.0 * np.log(u1)) * np.cos(2 * np.pi * u2)).reshape(shape), shape, dt)
     if k == "categorical_last":
         a = vf(op["a"])
         seed = int(v(op["seed"]).reshape(-1)[0]) & 0xFFFFFFFF

@@ -1,8 +1,11 @@
 """Per-op parity: each IR op kind runs through the C ABI on the GPU and is
 compared with the oracle on the same seeded inputs. Tolerance for f32:
-|gpu - ref| <= 1e-4 * max(|ref|, 1e-3 * max|ref|) per element (plus a 1e-7
-absolute floor for exact zeros); i32 outputs and dropout masks must match
-bit for bit."""
+|gpu - ref| <= 1e-4 * max(|ref|, 1e-2 * max|ref|) per element (plus a 1e-7
+absolute floor for exact zeros). The oracle accumulates in f64 and the GPU in
+f32, so an element that is the small difference of large terms carries an
+absolute error proportional to the tensor's magnitude, not its own; the
+1e-2 * max|ref| floor bounds it there. i32 outputs and dropout masks must
+match bit for bit."""
 import numpy as np
 import pytest
 
@@ -19,10 +22,10 @@ pytestmark = pytest.mark.gpu
 RTOL = 1e-4
 
 
-def close(gpu, ref, rtol=RTOL, floor=1e-7):
+def close(gpu, ref, rtol=RTOL, floor=1e-7, tensor_frac=1e-2):
     gpu = np.asarray(gpu, np.float64)
     ref = np.asarray(ref, np.float64)
-    scale = np.maximum(np.abs(ref), 1e-3 * max(np.abs(ref).max(), 1e-30))
+    scale = np.maximum(np.abs(ref), tensor_frac * max(np.abs(ref).max(), 1e-30))
     err = np.abs(gpu - ref)
     ok = err <= rtol * scale + floor
     i = int(np.argmax(err / (scale + 1e-30)))
