@@ -98,6 +98,10 @@ int tg_launch_list(tg_ctx* ctx, int graph_id, char* buf, size_t cap, size_t* nee
  * writes per-launch milliseconds (in tg_launch_list order). */
 int tg_profile_step(tg_ctx* ctx, int graph_id, float* ms_out, int cap, int* n_out);
 
+/* Error code recorded by a tcgen05 GEMM whose bounded barrier wait ran out
+ * (0 = none); reset != 0 clears it. (new: kernel health check for tests) */
+int tg_debug_gemm_error(int reset);
+
 const char* tg_last_error_name(void);
 const char* tg_last_error_message(void);
 

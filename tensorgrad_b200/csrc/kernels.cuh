@@ -136,6 +136,8 @@ struct GemmDesc {
 void launch_gemm_simt(const GemmDesc& g, cudaStream_t s);
 // tcgen05/TMEM 3xTF32 GEMM; returns false when the shape/layout is not taken.
 bool launch_gemm_tc(const GemmDesc& g, cudaStream_t s);
+// Error code a tcgen05 GEMM recorded after a bounded wait ran out (0 = none).
+int gemm_tc_error_flag(bool reset);
 
 // Embedding gather: out[r, :] = table[idx[r], :] (0 where idx out of range).
 void launch_gather_rows(const int* idx, const float* table, float* out, int64_t rows, int64_t V,

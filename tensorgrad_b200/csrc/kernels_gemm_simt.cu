@@ -77,7 +77,4 @@ void launch_gemm_simt(const GemmDesc& g, cudaStream_t s) {
   sgemm_kernel<<<grid, 256, 0, s>>>(g);
 }
 
-// Until the tcgen05 path lands every contraction takes the SIMT kernel.
-bool launch_gemm_tc(const GemmDesc&, cudaStream_t) { return false; }
-
 }  // namespace tg

@@ -1,0 +1,393 @@
+// f32 GEMM on the 5th-generation tensor cores with a 3xTF32 split.
+//
+// Replaces the reference's matmul / matmul_batched kernels
+// (src/codegen.ts:496-601, 16x16 shared-memory tiles of scalar f32 FMA) for
+// every contraction whose operands TMA can describe.
+//
+// Accuracy: each f32 operand x is split into hi = x with the low 13 mantissa
+// bits cleared (exactly representable in TF32) and lo = x - hi (exact in
+// f32, then truncated to TF32 by the tensor core). The product is
+// accumulated as lo_a*hi_b + hi_a*lo_b + hi_a*hi_b in one f32 TMEM
+// accumulator; the dropped lo_a*lo_b term and the truncation of lo are
+// ~2^-20 relative, so results match an f32 GEMM to ~1e-6.
+//
+// Structure (one CTA per 128x128 output tile, 192 threads):
+//   warp 0     TMA producer: per 32-deep K stage loads the A and B tiles
+//              (128B-swizzled, K-major or MN-major boxes) into a 3-stage ring
+//   warp 1     allocates TMEM (128 f32 columns), issues the tcgen05.mma
+//              instructions (M=128, N=128, K=8, kind::tf32) from one thread,
+//              commits each stage back to the producer
+//   warps 2-5  split each landed stage into hi (in place) and lo (a twin
+//              buffer with the same swizzled layout), then run the epilogue:
+//              tcgen05.ld the accumulator and store alpha*acc (+bias) (+C)
+// Every mbarrier wait is bounded; on timeout the kernel records an error
+// code in g_gemm_tc_error and leaves without further waits.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include <cstdio>
+#include <cstring>
+
+#include "kernels.cuh"
+
+namespace tg {
+
+__device__ int g_gemm_tc_error = 0;
+
+constexpr int TC_BM = 128, TC_BN = 128, TC_BK = 32, TC_STAGES = 3;
+constexpr int TC_TILE_BYTES = 128 * TC_BK * 4;           // 16 KB per operand tile
+constexpr int TC_STAGE_BYTES = 4 * TC_TILE_BYTES;        // A_hi, B_hi, A_lo, B_lo
+constexpr int TC_SMEM = TC_STAGES * TC_STAGE_BYTES + 1024 + 256;
+constexpr uint32_t TC_TMEM_COLS = 128;
+constexpr long long TC_SPIN_LIMIT = 1ll << 22;
+
+struct TcParams {
+  int64_t M, N, K;
+  int64_t batch, batch2;
+  int a_kmajor, b_kmajor;
+  int a_b1, a_b2, b_b1, b_b2;  // 1 when that operand varies with the batch index
+  float* C;
+  int64_t ldc, c_batch, c_batch2;
+  const float* bias;
+  float alpha;
+  int accumulate;
+};
+
+// ------------------------------------------------------------- PTX helpers --
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return (uint32_t)__cvta_generic_to_shared(p);
+}
+__device__ __forceinline__ void mbar_init(uint64_t* b, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(b)), "r"(count));
+}
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* b, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(b)), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint64_t* b) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(b)) : "memory");
+}
+__device__ __forceinline__ bool mbar_try(uint64_t* b, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(ok) : "r"(smem_u32(b)), "r"(parity) : "memory");
+  return ok != 0;
+}
+// Bounded wait: false (and an error code recorded) after TC_SPIN_LIMIT tries.
+__device__ __forceinline__ bool mbar_wait(uint64_t* b, uint32_t parity, int code) {
+  for (long long i = 0; i < TC_SPIN_LIMIT; ++i)
+    if (mbar_try(b, parity)) return true;
+  atomicExch(&g_gemm_tc_error, code);
+  return false;
+}
+__device__ __forceinline__ void tma_load_4d(const CUtensorMap* tm, uint64_t* bar, void* dst, int c0, int c1, int c2,
+                                            int c3) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4, %5}], [%6];"
+      ::"r"(smem_u32(dst)), "l"(tm), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(smem_u32(bar))
+      : "memory");
+}
+__device__ __forceinline__ uint64_t umma_desc(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
+  uint64_t d = 0;
+  d |= (uint64_t)((saddr >> 4) & 0x3FFF);
+  d |= (uint64_t)((lbo >> 4) & 0x3FFF) << 16;
+  d |= (uint64_t)((sbo >> 4) & 0x3FFF) << 32;
+  d |= (uint64_t)1 << 46;  // descriptor version for sm_100
+  d |= (uint64_t)2 << 61;  // 128-byte swizzle
+  return d;
+}
+__device__ __forceinline__ void umma_tf32(uint32_t tmem_d, uint64_t da, uint64_t db, uint32_t idesc, uint32_t acc) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+      " tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n}\n"
+      ::"r"(tmem_d), "l"(da), "l"(db), "r"(idesc), "r"(acc));
+}
+__device__ __forceinline__ void umma_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+               : "memory");
+}
+
+// ------------------------------------------------------------------ kernel --
+__global__ void __launch_bounds__(192, 1) gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA,
+                                                         const __grid_constant__ CUtensorMap tmB,
+                                                         const __grid_constant__ TcParams P) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + TC_STAGES * TC_STAGE_BYTES);
+  uint64_t* conv = full + TC_STAGES;
+  uint64_t* empty = conv + TC_STAGES;
+  uint64_t* accb = empty + TC_STAGES;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(accb + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t n0 = (int64_t)blockIdx.x * TC_BN, m0 = (int64_t)blockIdx.y * TC_BM;
+  const int64_t z = blockIdx.z;
+  const int i1 = (int)(z / P.batch2), i2 = (int)(z % P.batch2);
+  const int nk = (int)((P.K + TC_BK - 1) / TC_BK);
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < TC_STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&conv[s], 128);
+      mbar_init(&empty[s], 1);
+    }
+    mbar_init(accb, 1);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                 "r"(TC_TMEM_COLS));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+  }
+  __syncthreads();
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+  const uint32_t tmem = *tmem_slot;
+  bool ok = true;
+
+  if (warp == 0) {
+    // ---------------------------------------------------------- producer --
+    if (lane == 0) {
+      const int ab1 = P.a_b1 ? i1 : 0, ab2 = P.a_b2 ? i2 : 0;
+      const int bb1 = P.b_b1 ? i1 : 0, bb2 = P.b_b2 ? i2 : 0;
+      for (int it = 0; it < nk && ok; ++it) {
+        const int s = it % TC_STAGES;
+        const uint32_t ph = (uint32_t)(it / TC_STAGES) & 1u;
+        if (it >= TC_STAGES && !mbar_wait(&empty[s], ph ^ 1u, 1)) { ok = false; break; }
+        uint8_t* st = smem + s * TC_STAGE_BYTES;
+        mbar_expect_tx(&full[s], 2 * TC_TILE_BYTES);
+        const int k0 = it * TC_BK;
+        if (P.a_kmajor) tma_load_4d(&tmA, &full[s], st, k0, (int)m0, ab1, ab2);
+        else for (int j = 0; j < 4; ++j) tma_load_4d(&tmA, &full[s], st + j * 4096, (int)m0 + 32 * j, k0, ab1, ab2);
+        uint8_t* sb = st + TC_TILE_BYTES;
+        if (P.b_kmajor) tma_load_4d(&tmB, &full[s], sb, k0, (int)n0, bb1, bb2);
+        else for (int j = 0; j < 4; ++j) tma_load_4d(&tmB, &full[s], sb + j * 4096, (int)n0 + 32 * j, k0, bb1, bb2);
+      }
+    }
+  } else if (warp == 1) {
+    // --------------------------------------------------------------- MMA --
+    if (lane == 0) {
+      // kind::tf32 instruction descriptor: D f32, A/B tf32, majors, N>>3, M>>4
+      uint32_t idesc = (1u << 4) | (2u << 7) | (2u << 10) | ((P.a_kmajor ? 0u : 1u) << 15) |
+                       ((P.b_kmajor ? 0u : 1u) << 16) | ((uint32_t)(TC_BN >> 3) << 17) |
+                       ((uint32_t)(TC_BM >> 4) << 24);
+      for (int it = 0; it < nk && ok; ++it) {
+        const int s = it % TC_STAGES;
+        const uint32_t ph = (uint32_t)(it / TC_STAGES) & 1u;
+        if (!mbar_wait(&conv[s], ph, 2)) { ok = false; break; }
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+        const uint32_t base = smem_u32(smem + s * TC_STAGE_BYTES);
+        const uint32_t a_hi = base, b_hi = base + TC_TILE_BYTES;
+        const uint32_t a_lo = base + 2 * TC_TILE_BYTES, b_lo = base + 3 * TC_TILE_BYTES;
+#pragma unroll
+        for (int kk = 0; kk < TC_BK / 8; ++kk) {
+          // K-major: advance 32 bytes inside the 128-byte swizzle row;
+          // MN-major: advance one 8-row group (1024 bytes).
+          const uint32_t aoff = P.a_kmajor ? kk * 32 : kk * 1024;
+          const uint32_t boff = P.b_kmajor ? kk * 32 : kk * 1024;
+          const uint32_t a_lbo = P.a_kmajor ? 16 : 4096, b_lbo = P.b_kmajor ? 16 : 4096;
+          uint64_t dAh = umma_desc(a_hi + aoff, a_lbo, 1024), dAl = umma_desc(a_lo + aoff, a_lbo, 1024);
+          uint64_t dBh = umma_desc(b_hi + boff, b_lbo, 1024), dBl = umma_desc(b_lo + boff, b_lbo, 1024);
+          const uint32_t first = (it == 0 && kk == 0) ? 0u : 1u;
+          umma_tf32(tmem, dAl, dBh, idesc, first);
+          umma_tf32(tmem, dAh, dBl, idesc, 1u);
+          umma_tf32(tmem, dAh, dBh, idesc, 1u);
+        }
+        umma_commit(&empty[s]);  // frees the stage once these MMAs have read it
+      }
+      if (ok) umma_commit(accb);
+    }
+  } else {
+    // ------------------------------------------------ split, then epilogue --
+    const int t = threadIdx.x - 64;  // 0..127
+    for (int it = 0; it < nk && ok; ++it) {
+      const int s = it % TC_STAGES;
+      const uint32_t ph = (uint32_t)(it / TC_STAGES) & 1u;
+      if (!mbar_wait(&full[s], ph, 3)) { ok = false; break; }
+      uint8_t* st = smem + s * TC_STAGE_BYTES;
+      float4* hi = reinterpret_cast<float4*>(st);
+      float4* lo = reinterpret_cast<float4*>(st + 2 * TC_TILE_BYTES);
+#pragma unroll 4
+      for (int q = t; q < 2 * TC_TILE_BYTES / 16; q += 128) {
+        float4 x = hi[q];
+        float* xv = &x.x;
+        float4 h, l;
+        float* hv = &h.x;
+        float* lv = &l.x;
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          float hh = __uint_as_float(__float_as_uint(xv[e]) & 0xFFFFE000u);
+          hv[e] = hh;
+          lv[e] = xv[e] - hh;
+        }
+        hi[q] = h;
+        lo[q] = l;
+      }
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      mbar_arrive(&conv[s]);
+    }
+    if (ok && mbar_wait(accb, 0, 4)) {
+      asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+      const int g = warp & 3;  // TMEM lane group this warp may access
+      const int64_t row = m0 + g * 32 + lane;
+      float* C = P.C + (int64_t)i1 * P.c_batch + (int64_t)i2 * P.c_batch2;
+#pragma unroll 1
+      for (int c = 0; c < TC_BN / 32; ++c) {
+        uint32_t r[32];
+        const uint32_t taddr = tmem + ((uint32_t)(g * 32) << 16) + (uint32_t)(c * 32);
+        asm volatile(
+            "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+            "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+            : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+              "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]),
+              "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]),
+              "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]),
+              "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+            : "r"(taddr));
+        asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+        if (row >= P.M) continue;
+        const int64_t col0 = n0 + c * 32;
+        float* dst = C + row * P.ldc + col0;
+        const bool full_vec = (col0 + 32 <= P.N) && ((P.ldc & 3) == 0) && ((reinterpret_cast<uintptr_t>(dst) & 15) == 0);
+        if (full_vec) {
+#pragma unroll
+          for (int j = 0; j < 32; j += 4) {
+            float4 v = make_float4(__uint_as_float(r[j]), __uint_as_float(r[j + 1]), __uint_as_float(r[j + 2]),
+                                   __uint_as_float(r[j + 3]));
+            v.x *= P.alpha; v.y *= P.alpha; v.z *= P.alpha; v.w *= P.alpha;
+            if (P.bias) {
+              v.x += P.bias[col0 + j]; v.y += P.bias[col0 + j + 1];
+              v.z += P.bias[col0 + j + 2]; v.w += P.bias[col0 + j + 3];
+            }
+            float4* d4 = reinterpret_cast<float4*>(dst + j);
+            if (P.accumulate) {
+              float4 o = *d4;
+              v.x += o.x; v.y += o.y; v.z += o.z; v.w += o.w;
+            }
+            *d4 = v;
+          }
+        } else {
+#pragma unroll
+          for (int j = 0; j < 32; ++j) {
+            if (col0 + j >= P.N) break;
+            float v = __uint_as_float(r[j]) * P.alpha;
+            if (P.bias) v += P.bias[col0 + j];
+            if (P.accumulate) v += dst[j];
+            dst[j] = v;
+          }
+        }
+      }
+      asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+    }
+  }
+  __syncthreads();
+  if (warp == 1) {
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TC_TMEM_COLS));
+  }
+}
+
+// ------------------------------------------------------------------- host --
+static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static bool tried = false;
+  if (!tried) {
+    tried = true;
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  }
+  return fn;
+}
+
+// Tensor map for one operand. kmajor: dims {K, MN, b1, b2}; else {MN, K, b1, b2}.
+static bool make_map(CUtensorMap* tm, const float* base, bool kmajor, int64_t mn, int64_t k, int64_t ld_mn,
+                     int64_t ld_k, int64_t e1, int64_t s1, int64_t e2, int64_t s2) {
+  auto fn = encode_fn();
+  if (!fn) return false;
+  cuuint64_t dims[4], strides[3];
+  cuuint32_t box[4], estr[4] = {1, 1, 1, 1};
+  if (kmajor) {
+    dims[0] = (cuuint64_t)k; dims[1] = (cuuint64_t)mn; strides[0] = (cuuint64_t)(ld_mn * 4);
+    box[0] = TC_BK; box[1] = 128;
+  } else {
+    dims[0] = (cuuint64_t)mn; dims[1] = (cuuint64_t)k; strides[0] = (cuuint64_t)(ld_k * 4);
+    box[0] = 32; box[1] = TC_BK;
+  }
+  dims[2] = (cuuint64_t)e1; dims[3] = (cuuint64_t)e2;
+  strides[1] = (cuuint64_t)((e1 > 1 ? s1 : 1) * 4);
+  strides[2] = (cuuint64_t)((e2 > 1 ? s2 : 1) * 4);
+  box[2] = 1; box[3] = 1;
+  for (int i = 0; i < 3; ++i) {
+    if (strides[i] % 16 != 0 || strides[i] == 0) {
+      // unit-extent batch dims may use any stride: round it up to a legal value
+      if ((i >= 1) && dims[i + 1] == 1) strides[i] = 16;
+      else return false;
+    }
+  }
+  CUresult r = fn(tm, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, const_cast<float*>(base), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
+static bool tc_enabled() {
+  static int v = -1;
+  if (v < 0) {
+    const char* e = getenv("TG_GEMM_TC");
+    v = (e && e[0] == '0') ? 0 : 1;
+  }
+  return v == 1;
+}
+
+bool launch_gemm_tc(const GemmDesc& g, cudaStream_t s) {
+  if (!tc_enabled()) return false;
+  // Tiny contractions are cheaper on CUDA cores than a 128x128 tile pipeline.
+  if (g.M * g.N * g.K < (int64_t)64 * 64 * 64 || g.K < 16) return false;
+  const bool a_k = g.lda_k == 1, a_mn = g.lda_m == 1;
+  const bool b_k = g.ldb_k == 1, b_mn = g.ldb_n == 1;
+  if (!(a_k || a_mn) || !(b_k || b_mn)) return false;
+  if ((reinterpret_cast<uintptr_t>(g.A) & 15) || (reinterpret_cast<uintptr_t>(g.B) & 15)) return false;
+  if (g.M > INT32_MAX || g.N > INT32_MAX || g.K > INT32_MAX) return false;
+  const int64_t b2 = g.batch2 > 0 ? g.batch2 : 1;
+  const int64_t b1 = g.batch / b2;
+  CUtensorMap ta, tb;
+  const bool ak = a_k;  // prefer K-major when both hold (degenerate dims)
+  const bool bk = b_k;
+  if (!make_map(&ta, g.A, ak, g.M, g.K, g.lda_m, g.lda_k, g.a_batch ? b1 : 1, g.a_batch, g.a_batch2 ? b2 : 1,
+                g.a_batch2))
+    return false;
+  if (!make_map(&tb, g.B, bk, g.N, g.K, g.ldb_n, g.ldb_k, g.b_batch ? b1 : 1, g.b_batch, g.b_batch2 ? b2 : 1,
+                g.b_batch2))
+    return false;
+  TcParams p{};
+  p.M = g.M; p.N = g.N; p.K = g.K;
+  p.batch = g.batch; p.batch2 = b2;
+  p.a_kmajor = ak ? 1 : 0; p.b_kmajor = bk ? 1 : 0;
+  p.a_b1 = g.a_batch ? 1 : 0; p.a_b2 = g.a_batch2 ? 1 : 0;
+  p.b_b1 = g.b_batch ? 1 : 0; p.b_b2 = g.b_batch2 ? 1 : 0;
+  p.C = g.C; p.ldc = g.ldc; p.c_batch = g.c_batch; p.c_batch2 = g.c_batch2;
+  p.bias = g.bias; p.alpha = g.alpha; p.accumulate = g.accumulate;
+  static bool attr = false;
+  if (!attr) {
+    if (cudaFuncSetAttribute(gemm_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, TC_SMEM) != cudaSuccess)
+      return false;
+    attr = true;
+  }
+  dim3 grid((unsigned)((g.N + TC_BN - 1) / TC_BN), (unsigned)((g.M + TC_BM - 1) / TC_BM), (unsigned)g.batch);
+  gemm_tc_kernel<<<grid, 192, TC_SMEM, s>>>(ta, tb, p);
+  return true;
+}
+
+int gemm_tc_error_flag(bool reset) {
+  int v = 0;
+  cudaMemcpyFromSymbol(&v, g_gemm_tc_error, sizeof(int));
+  if (reset) {
+    int z = 0;
+    cudaMemcpyToSymbol(g_gemm_tc_error, &z, sizeof(int));
+  }
+  return v;
+}
+
+}  // namespace tg

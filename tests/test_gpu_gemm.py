@@ -1,0 +1,51 @@
+"""tcgen05 3xTF32 GEMM parity: every operand layout the planner produces
+(A and B each K-major or MN-major), ragged tiles, batched head views, and a
+large-K reduction, against the f64 oracle at the op tolerance."""
+import numpy as np
+import pytest
+
+import tensorgrad_b200 as tg
+from tensorgrad_b200.trace import tensor_input as T
+
+from .test_gpu_ops import rnd, run
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.mark.parametrize("ta,tb", [(False, False), (False, True), (True, False), (True, True)])
+@pytest.mark.parametrize("M,K,N", [(300, 200, 260), (128, 64, 128), (1000, 96, 70)])
+def test_gemm_layouts(ctx, ta, tb, M, K, N):
+    a = rnd([K, M] if ta else [M, K], 40)
+    b = rnd([N, K] if tb else [K, N], 41)
+
+    def build():
+        A = T("a", list(a.shape))
+        B = T("b", list(b.shape))
+        return tg.matmul(tg.swapAxes(A, 0, 1) if ta else A, tg.swapAxes(B, 0, 1) if tb else B)
+    run(ctx, build, {"a": a, "b": b})
+
+
+def test_gemm_attention_views(ctx):
+    B_, Tn, H, d = 2, 128, 3, 64
+    x = rnd([B_, Tn, H * d], 42)
+    y = rnd([B_, Tn, H * d], 43)
+
+    def build():
+        q = tg.splitHeads(T("x", [B_, Tn, H * d]), H)
+        k = tg.splitHeads(T("y", [B_, Tn, H * d]), H)
+        s = tg.mul(tg.matmul(q, tg.swapAxes(k, -1, -2)), 0.125)
+        return tg.mergeHeads(tg.matmul(s, k))
+    run(ctx, build, {"x": x, "y": y})
+
+
+def test_gemm_long_k_weight_grad_shape(ctx):
+    x = rnd([8192, 96], 44)
+    dy = rnd([8192, 160], 45)
+    run(ctx, lambda: tg.matmul(tg.swapAxes(T("x", [8192, 96]), 0, 1), T("dy", [8192, 160])), {"x": x, "dy": dy})
+
+
+def test_gemm_tc_error_flag_clear(ctx):
+    import ctypes
+    from tensorgrad_b200 import backend as BK
+    lib = BK.load()
+    assert lib.tg_debug_gemm_error(1) == 0
