@@ -101,6 +101,8 @@ int tg_profile_step(tg_ctx* ctx, int graph_id, float* ms_out, int cap, int* n_ou
 /* Error code recorded by a tcgen05 GEMM whose bounded barrier wait ran out
  * (0 = none); reset != 0 clears it. (new: kernel health check for tests) */
 int tg_debug_gemm_error(int reset);
+/* Progress markers of the first GEMM tile (8 ints) for pipeline diagnosis. */
+int tg_debug_gemm_dbg(int* out8);
 
 const char* tg_last_error_name(void);
 const char* tg_last_error_message(void);

@@ -13,7 +13,9 @@
 //
 // Structure (one CTA per 128x128 output tile, 192 threads):
 //   warp 0     TMA producer: per 32-deep K stage loads the A and B tiles
-//              (128B-swizzled, K-major or MN-major boxes) into a 3-stage ring
+//              (128B-swizzled; K-major: one 128x32 box; MN-major: sixteen
+//              8(K)x32(MN) boxes in UMMA's canonical MN-major atom order)
+//              into a 3-stage ring
 //   warp 1     allocates TMEM (128 f32 columns), issues the tcgen05.mma
 //              instructions (M=128, N=128, K=8, kind::tf32) from one thread,
 //              commits each stage back to the producer
@@ -33,10 +35,16 @@
 namespace tg {
 
 __device__ int g_gemm_tc_error = 0;
+// Progress markers of CTA (0,0,0) for diagnosing a stalled pipeline:
+// [0] producer stages issued, [1] stages split, [2] MMA stages issued,
+// [3] epilogue reached, [4] tmem base address, [5] last error code.
+__device__ int g_gemm_tc_dbg[8];
 
-constexpr int TC_BM = 128, TC_BN = 128, TC_BK = 32, TC_STAGES = 3;
+constexpr int TC_BM = 128, TC_BN = 128, TC_BK = 32, TC_STAGES = 2;
 constexpr int TC_TILE_BYTES = 128 * TC_BK * 4;           // 16 KB per operand tile
-constexpr int TC_STAGE_BYTES = 4 * TC_TILE_BYTES;        // A_hi, B_hi, A_lo, B_lo
+// A_hi, B_hi, A_lo, B_lo (K-major, what the MMA reads) + A/B staging for
+// MN-major operands (what TMA writes when the operand is not K-major)
+constexpr int TC_STAGE_BYTES = 6 * TC_TILE_BYTES;
 constexpr int TC_SMEM = TC_STAGES * TC_STAGE_BYTES + 1024 + 256;
 constexpr uint32_t TC_TMEM_COLS = 128;
 constexpr long long TC_SPIN_LIMIT = 1ll << 22;
@@ -51,6 +59,7 @@ struct TcParams {
   const float* bias;
   float alpha;
   int accumulate;
+  int dbg;  // 1: pre-fill the accumulator with 7.0 and accumulate onto it (diagnostic)
 };
 
 // ------------------------------------------------------------- PTX helpers --
@@ -97,10 +106,12 @@ __device__ __forceinline__ uint64_t umma_desc(uint32_t saddr, uint32_t lbo, uint
   return d;
 }
 __device__ __forceinline__ void umma_tf32(uint32_t tmem_d, uint64_t da, uint64_t db, uint32_t idesc, uint32_t acc) {
+  // The disable-output-lane mask is given explicitly (all lanes enabled).
+  const uint32_t z = 0;
   asm volatile(
       "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
-      " tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n}\n"
-      ::"r"(tmem_d), "l"(da), "l"(db), "r"(idesc), "r"(acc));
+      " tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, {%5, %6, %7, %8}, p;\n}\n"
+      ::"r"(tmem_d), "l"(da), "l"(db), "r"(idesc), "r"(acc), "r"(z), "r"(z), "r"(z), "r"(z));
 }
 __device__ __forceinline__ void umma_commit(uint64_t* bar) {
   asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
@@ -143,6 +154,22 @@ __global__ void __launch_bounds__(192, 1) gemm_tc_kernel(const __grid_constant__
   asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
   const uint32_t tmem = *tmem_slot;
   bool ok = true;
+  if (P.dbg == 1) {
+    if (warp >= 2) {
+      uint32_t v = __float_as_uint(7.0f);
+      const int g = warp & 3;
+      for (int c = 0; c < 4; ++c) {
+        const uint32_t taddr = tmem + ((uint32_t)(g * 32) << 16) + (uint32_t)(c * 32);
+        asm volatile(
+            "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,"
+            "%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1};" ::"r"(taddr), "r"(v));
+      }
+      asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+    }
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+    __syncthreads();
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+  }
 
   if (warp == 0) {
     // ---------------------------------------------------------- producer --
@@ -157,18 +184,21 @@ __global__ void __launch_bounds__(192, 1) gemm_tc_kernel(const __grid_constant__
         mbar_expect_tx(&full[s], 2 * TC_TILE_BYTES);
         const int k0 = it * TC_BK;
         if (P.a_kmajor) tma_load_4d(&tmA, &full[s], st, k0, (int)m0, ab1, ab2);
-        else for (int j = 0; j < 4; ++j) tma_load_4d(&tmA, &full[s], st + j * 4096, (int)m0 + 32 * j, k0, ab1, ab2);
+        else for (int j = 0; j < 4; ++j)
+          tma_load_4d(&tmA, &full[s], st + 4 * TC_TILE_BYTES + j * 4096, (int)m0 + 32 * j, k0, ab1, ab2);
         uint8_t* sb = st + TC_TILE_BYTES;
         if (P.b_kmajor) tma_load_4d(&tmB, &full[s], sb, k0, (int)n0, bb1, bb2);
-        else for (int j = 0; j < 4; ++j) tma_load_4d(&tmB, &full[s], sb + j * 4096, (int)n0 + 32 * j, k0, bb1, bb2);
+        else for (int j = 0; j < 4; ++j)
+          tma_load_4d(&tmB, &full[s], st + 5 * TC_TILE_BYTES + j * 4096, (int)n0 + 32 * j, k0, bb1, bb2);
+        if (blockIdx.x == 0 && blockIdx.y == 0 && blockIdx.z == 0) g_gemm_tc_dbg[0] = it + 1;
       }
     }
   } else if (warp == 1) {
     // --------------------------------------------------------------- MMA --
     if (lane == 0) {
       // kind::tf32 instruction descriptor: D f32, A/B tf32, majors, N>>3, M>>4
-      uint32_t idesc = (1u << 4) | (2u << 7) | (2u << 10) | ((P.a_kmajor ? 0u : 1u) << 15) |
-                       ((P.b_kmajor ? 0u : 1u) << 16) | ((uint32_t)(TC_BN >> 3) << 17) |
+      // (both operands are K-major in shared memory after the split pass)
+      uint32_t idesc = (1u << 4) | (2u << 7) | (2u << 10) | ((uint32_t)(TC_BN >> 3) << 17) |
                        ((uint32_t)(TC_BM >> 4) << 24);
       for (int it = 0; it < nk && ok; ++it) {
         const int s = it % TC_STAGES;
@@ -180,19 +210,18 @@ __global__ void __launch_bounds__(192, 1) gemm_tc_kernel(const __grid_constant__
         const uint32_t a_lo = base + 2 * TC_TILE_BYTES, b_lo = base + 3 * TC_TILE_BYTES;
 #pragma unroll
         for (int kk = 0; kk < TC_BK / 8; ++kk) {
-          // K-major: advance 32 bytes inside the 128-byte swizzle row;
-          // MN-major: advance one 8-row group (1024 bytes).
-          const uint32_t aoff = P.a_kmajor ? kk * 32 : kk * 1024;
-          const uint32_t boff = P.b_kmajor ? kk * 32 : kk * 1024;
-          const uint32_t a_lbo = P.a_kmajor ? 16 : 4096, b_lbo = P.b_kmajor ? 16 : 4096;
-          uint64_t dAh = umma_desc(a_hi + aoff, a_lbo, 1024), dAl = umma_desc(a_lo + aoff, a_lbo, 1024);
-          uint64_t dBh = umma_desc(b_hi + boff, b_lbo, 1024), dBl = umma_desc(b_lo + boff, b_lbo, 1024);
-          const uint32_t first = (it == 0 && kk == 0) ? 0u : 1u;
+          // K-major tiles: 128 rows of 128 bytes (32 K values), 8-row groups
+          // 1 KB apart (SBO); a K step of 8 advances 32 bytes in the row.
+          const uint32_t off = kk * 32;
+          uint64_t dAh = umma_desc(a_hi + off, 16, 1024), dAl = umma_desc(a_lo + off, 16, 1024);
+          uint64_t dBh = umma_desc(b_hi + off, 16, 1024), dBl = umma_desc(b_lo + off, 16, 1024);
+          const uint32_t first = (it == 0 && kk == 0 && P.dbg != 1) ? 0u : 1u;
           umma_tf32(tmem, dAl, dBh, idesc, first);
           umma_tf32(tmem, dAh, dBl, idesc, 1u);
           umma_tf32(tmem, dAh, dBh, idesc, 1u);
         }
         umma_commit(&empty[s]);  // frees the stage once these MMAs have read it
+        if (blockIdx.x == 0 && blockIdx.y == 0 && blockIdx.z == 0) g_gemm_tc_dbg[2] = it + 1;
       }
       if (ok) umma_commit(accb);
     }
@@ -204,29 +233,71 @@ __global__ void __launch_bounds__(192, 1) gemm_tc_kernel(const __grid_constant__
       const uint32_t ph = (uint32_t)(it / TC_STAGES) & 1u;
       if (!mbar_wait(&full[s], ph, 3)) { ok = false; break; }
       uint8_t* st = smem + s * TC_STAGE_BYTES;
-      float4* hi = reinterpret_cast<float4*>(st);
-      float4* lo = reinterpret_cast<float4*>(st + 2 * TC_TILE_BYTES);
+#pragma unroll 1
+      for (int op = 0; op < 2; ++op) {
+        const bool kmaj = op == 0 ? P.a_kmajor : P.b_kmajor;
+        uint8_t* hi_t = st + op * TC_TILE_BYTES;
+        uint8_t* lo_t = st + (2 + op) * TC_TILE_BYTES;
+        if (kmaj) {
+          // landed K-major: split in place, lo into the twin buffer (same layout)
+          float4* hi = reinterpret_cast<float4*>(hi_t);
+          float4* lo = reinterpret_cast<float4*>(lo_t);
 #pragma unroll 4
-      for (int q = t; q < 2 * TC_TILE_BYTES / 16; q += 128) {
-        float4 x = hi[q];
-        float* xv = &x.x;
-        float4 h, l;
-        float* hv = &h.x;
-        float* lv = &l.x;
+          for (int q = t; q < TC_TILE_BYTES / 16; q += 128) {
+            float4 x = hi[q], h, l;
+            const float* xv = &x.x;
+            float* hv = &h.x;
+            float* lv = &l.x;
 #pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          float hh = __uint_as_float(__float_as_uint(xv[e]) & 0xFFFFE000u);
-          hv[e] = hh;
-          lv[e] = xv[e] - hh;
+            for (int e = 0; e < 4; ++e) {
+              float hh = __uint_as_float(__float_as_uint(xv[e]) & 0xFFFFE000u);
+              hv[e] = hh;
+              lv[e] = xv[e] - hh;
+            }
+            hi[q] = h;
+            lo[q] = l;
+          }
+        } else {
+          // landed MN-major in staging: 4 boxes (MN chunk j) of 32 K-rows x
+          // 128 bytes; element (k, mn) sits in row k, 16-byte chunk
+          // (mn%32)/4 XOR (k%8). Write hi/lo transposed into the K-major
+          // tiles: element (mn, k) in row mn, chunk (k/4) XOR (mn%8).
+          const uint8_t* stg = st + (4 + op) * TC_TILE_BYTES;
+#pragma unroll 2
+          for (int q = t; q < TC_TILE_BYTES / 16; q += 128) {
+            const int j = q >> 8;          // MN chunk (256 float4 per 4 KB box)
+            const int k = (q >> 3) & 31;   // K row inside the box
+            const int pc = q & 7;          // physical 16-byte chunk
+            const int lc = pc ^ (k & 7);   // logical chunk -> mn = 4*lc .. 4*lc+3
+            const float4 x = *reinterpret_cast<const float4*>(stg + q * 16);
+            const float* xv = &x.x;
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              const int mn = j * 32 + lc * 4 + e;
+              const uint32_t o = (uint32_t)mn * 128u + (uint32_t)((((k >> 2) ^ (mn & 7)) << 4) + ((k & 3) << 2));
+              const float hh = __uint_as_float(__float_as_uint(xv[e]) & 0xFFFFE000u);
+              *reinterpret_cast<float*>(hi_t + o) = hh;
+              *reinterpret_cast<float*>(lo_t + o) = xv[e] - hh;
+            }
+          }
         }
-        hi[q] = h;
-        lo[q] = l;
       }
       asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
       mbar_arrive(&conv[s]);
+      if (t == 0 && blockIdx.x == 0 && blockIdx.y == 0 && blockIdx.z == 0) {
+        g_gemm_tc_dbg[1] = it + 1;
+        if (it == 0) {
+          g_gemm_tc_dbg[5] = __float_as_int(reinterpret_cast<float*>(st)[0]);  // A_hi (0,0)
+          g_gemm_tc_dbg[6] = __float_as_int(reinterpret_cast<float*>(st + TC_TILE_BYTES)[0]);
+        }
+      }
     }
     if (ok && mbar_wait(accb, 0, 4)) {
       asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+      if (t == 0 && blockIdx.x == 0 && blockIdx.y == 0 && blockIdx.z == 0) {
+        g_gemm_tc_dbg[3] = 1;
+        g_gemm_tc_dbg[4] = (int)tmem;
+      }
       const int g = warp & 3;  // TMEM lane group this warp may access
       const int64_t row = m0 + g * 32 + lane;
       float* C = P.C + (int64_t)i1 * P.c_batch + (int64_t)i2 * P.c_batch2;
@@ -244,6 +315,7 @@ __global__ void __launch_bounds__(192, 1) gemm_tc_kernel(const __grid_constant__
               "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
             : "r"(taddr));
         asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+        if (c == 0 && t == 0 && blockIdx.x == 0 && blockIdx.y == 0 && blockIdx.z == 0) g_gemm_tc_dbg[7] = (int)r[0];
         if (row >= P.M) continue;
         const int64_t col0 = n0 + c * 32;
         float* dst = C + row * P.ldc + col0;
@@ -369,6 +441,10 @@ bool launch_gemm_tc(const GemmDesc& g, cudaStream_t s) {
   p.b_b1 = g.b_batch ? 1 : 0; p.b_b2 = g.b_batch2 ? 1 : 0;
   p.C = g.C; p.ldc = g.ldc; p.c_batch = g.c_batch; p.c_batch2 = g.c_batch2;
   p.bias = g.bias; p.alpha = g.alpha; p.accumulate = g.accumulate;
+  {
+    const char* d = getenv("TG_GEMM_TC_DEBUG");
+    p.dbg = d ? atoi(d) : 0;
+  }
   static bool attr = false;
   if (!attr) {
     if (cudaFuncSetAttribute(gemm_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, TC_SMEM) != cudaSuccess)
@@ -378,6 +454,10 @@ bool launch_gemm_tc(const GemmDesc& g, cudaStream_t s) {
   dim3 grid((unsigned)((g.N + TC_BN - 1) / TC_BN), (unsigned)((g.M + TC_BM - 1) / TC_BM), (unsigned)g.batch);
   gemm_tc_kernel<<<grid, 192, TC_SMEM, s>>>(ta, tb, p);
   return true;
+}
+
+int gemm_tc_debug(int* out8) {
+  return cudaMemcpyFromSymbol(out8, g_gemm_tc_dbg, 8 * sizeof(int)) == cudaSuccess ? 0 : 1;
 }
 
 int gemm_tc_error_flag(bool reset) {
