@@ -19,9 +19,10 @@
 //   warp 1     allocates TMEM (128 f32 columns), issues the tcgen05.mma
 //              instructions (M=128, N=128, K=8, kind::tf32) from one thread,
 //              commits each stage back to the producer
-//   warps 2-5  split each landed stage into hi (in place) and lo (a twin
-//              buffer with the same swizzled layout), then run the epilogue:
-//              tcgen05.ld the accumulator and store alpha*acc (+bias) (+C)
+//   warps 2-5  split each landed stage into K-major hi and lo tiles (in
+//              place for K-major operands; transposed out of a staging box for
+//              MN-major ones), drain finished accumulator chunks into f32
+//              registers, then store alpha*acc (+bias) (+C)
 // Every mbarrier wait is bounded; on timeout the kernel records an error
 // code in g_gemm_tc_error and leaves without further waits.
 #include <cuda.h>
@@ -37,7 +38,7 @@ namespace tg {
 __device__ int g_gemm_tc_error = 0;
 // Progress markers of CTA (0,0,0) for diagnosing a stalled pipeline:
 // [0] producer stages issued, [1] stages split, [2] MMA stages issued,
-// [3] epilogue reached, [4] tmem base address, [5] last error code.
+// [3] epilogue reached.
 __device__ int g_gemm_tc_dbg[8];
 
 constexpr int TC_BM = 128, TC_BN = 128, TC_BK = 32, TC_STAGES = 2;
@@ -46,7 +47,7 @@ constexpr int TC_TILE_BYTES = 128 * TC_BK * 4;           // 16 KB per operand ti
 // MN-major operands (what TMA writes when the operand is not K-major)
 constexpr int TC_STAGE_BYTES = 6 * TC_TILE_BYTES;
 constexpr int TC_SMEM = TC_STAGES * TC_STAGE_BYTES + 1024 + 256;
-constexpr uint32_t TC_TMEM_COLS = 128;
+constexpr uint32_t TC_TMEM_COLS = 256;  // two 128-column accumulators
 constexpr long long TC_SPIN_LIMIT = 1ll << 22;
 
 struct TcParams {
@@ -59,7 +60,6 @@ struct TcParams {
   const float* bias;
   float alpha;
   int accumulate;
-  int dbg;  // 1: pre-fill the accumulator with 7.0 and accumulate onto it (diagnostic)
 };
 
 // ------------------------------------------------------------- PTX helpers --
@@ -119,6 +119,78 @@ __device__ __forceinline__ void umma_commit(uint64_t* bar) {
 }
 
 // ------------------------------------------------------------------ kernel --
+// Accumulator chunking: the tensor core accumulates in f32 without
+// round-to-nearest on every add, so error grows with the number of
+// accumulation steps. The MMA warp therefore alternates between two TMEM
+// accumulators every TC_CHUNK K-stages (384 MMA-K), and the split/epilogue
+// warps drain each finished accumulator into per-thread f32 registers with
+// round-to-nearest adds; total error then grows like sqrt(K) instead of K.
+constexpr int TC_CHUNK = 4;
+
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+        "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+        "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+}
+
+// Split one landed stage (both operands) into K-major hi/lo tiles.
+__device__ __forceinline__ void split_stage(uint8_t* st, int t, int a_kmajor, int b_kmajor) {
+#pragma unroll 1
+  for (int op = 0; op < 2; ++op) {
+    const bool kmaj = op == 0 ? a_kmajor : b_kmajor;
+    uint8_t* hi_t = st + op * TC_TILE_BYTES;
+    uint8_t* lo_t = st + (2 + op) * TC_TILE_BYTES;
+    if (kmaj) {
+      // landed K-major: split in place, lo into the twin buffer (same layout)
+      float4* hi = reinterpret_cast<float4*>(hi_t);
+      float4* lo = reinterpret_cast<float4*>(lo_t);
+#pragma unroll 4
+      for (int q = t; q < TC_TILE_BYTES / 16; q += 128) {
+        float4 x = hi[q], h, l;
+        const float* xv = &x.x;
+        float* hv = &h.x;
+        float* lv = &l.x;
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          float hh = __uint_as_float(__float_as_uint(xv[e]) & 0xFFFFE000u);
+          hv[e] = hh;
+          lv[e] = xv[e] - hh;
+        }
+        hi[q] = h;
+        lo[q] = l;
+      }
+    } else {
+      // landed MN-major in staging: 4 boxes (MN chunk j) of 32 K-rows x
+      // 128 bytes; element (k, mn) sits in row k, 16-byte chunk
+      // (mn%32)/4 XOR (k%8). Write hi/lo transposed into the K-major
+      // tiles: element (mn, k) in row mn, chunk (k/4) XOR (mn%8).
+      const uint8_t* stg = st + (4 + op) * TC_TILE_BYTES;
+#pragma unroll 2
+      for (int q = t; q < TC_TILE_BYTES / 16; q += 128) {
+        const int j = q >> 8;
+        const int k = (q >> 3) & 31;
+        const int pc = q & 7;
+        const int lc = pc ^ (k & 7);
+        const float4 x = *reinterpret_cast<const float4*>(stg + q * 16);
+        const float* xv = &x.x;
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int mn = j * 32 + lc * 4 + e;
+          const uint32_t o = (uint32_t)mn * 128u + (uint32_t)((((k >> 2) ^ (mn & 7)) << 4) + ((k & 3) << 2));
+          const float hh = __uint_as_float(__float_as_uint(xv[e]) & 0xFFFFE000u);
+          *reinterpret_cast<float*>(hi_t + o) = hh;
+          *reinterpret_cast<float*>(lo_t + o) = xv[e] - hh;
+        }
+      }
+    }
+  }
+}
+
 __global__ void __launch_bounds__(192, 1) gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA,
                                                          const __grid_constant__ CUtensorMap tmB,
                                                          const __grid_constant__ TcParams P) {
@@ -127,14 +199,17 @@ __global__ void __launch_bounds__(192, 1) gemm_tc_kernel(const __grid_constant__
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + TC_STAGES * TC_STAGE_BYTES);
   uint64_t* conv = full + TC_STAGES;
   uint64_t* empty = conv + TC_STAGES;
-  uint64_t* accb = empty + TC_STAGES;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(accb + 1);
+  uint64_t* dfull = empty + TC_STAGES;   // [2] accumulator chunk finished (MMA commit)
+  uint64_t* dempty = dfull + 2;          // [2] accumulator drained (128 epilogue threads)
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(dempty + 2);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int64_t n0 = (int64_t)blockIdx.x * TC_BN, m0 = (int64_t)blockIdx.y * TC_BM;
   const int64_t z = blockIdx.z;
   const int i1 = (int)(z / P.batch2), i2 = (int)(z % P.batch2);
   const int nk = (int)((P.K + TC_BK - 1) / TC_BK);
+  const int nchunks = (nk + TC_CHUNK - 1) / TC_CHUNK;
+  const bool first_cta = blockIdx.x == 0 && blockIdx.y == 0 && blockIdx.z == 0;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < TC_STAGES; ++s) {
@@ -142,7 +217,10 @@ __global__ void __launch_bounds__(192, 1) gemm_tc_kernel(const __grid_constant__
       mbar_init(&conv[s], 128);
       mbar_init(&empty[s], 1);
     }
-    mbar_init(accb, 1);
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&dfull[a], 1);
+      mbar_init(&dempty[a], 128);
+    }
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   if (warp == 1) {
@@ -154,22 +232,6 @@ __global__ void __launch_bounds__(192, 1) gemm_tc_kernel(const __grid_constant__
   asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
   const uint32_t tmem = *tmem_slot;
   bool ok = true;
-  if (P.dbg == 1) {
-    if (warp >= 2) {
-      uint32_t v = __float_as_uint(7.0f);
-      const int g = warp & 3;
-      for (int c = 0; c < 4; ++c) {
-        const uint32_t taddr = tmem + ((uint32_t)(g * 32) << 16) + (uint32_t)(c * 32);
-        asm volatile(
-            "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,"
-            "%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1};" ::"r"(taddr), "r"(v));
-      }
-      asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
-    }
-    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
-    __syncthreads();
-    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-  }
 
   if (warp == 0) {
     // ---------------------------------------------------------- producer --
@@ -186,28 +248,32 @@ __global__ void __launch_bounds__(192, 1) gemm_tc_kernel(const __grid_constant__
         if (P.a_kmajor) tma_load_4d(&tmA, &full[s], st, k0, (int)m0, ab1, ab2);
         else for (int j = 0; j < 4; ++j)
           tma_load_4d(&tmA, &full[s], st + 4 * TC_TILE_BYTES + j * 4096, (int)m0 + 32 * j, k0, ab1, ab2);
-        uint8_t* sb = st + TC_TILE_BYTES;
-        if (P.b_kmajor) tma_load_4d(&tmB, &full[s], sb, k0, (int)n0, bb1, bb2);
+        if (P.b_kmajor) tma_load_4d(&tmB, &full[s], st + TC_TILE_BYTES, k0, (int)n0, bb1, bb2);
         else for (int j = 0; j < 4; ++j)
           tma_load_4d(&tmB, &full[s], st + 5 * TC_TILE_BYTES + j * 4096, (int)n0 + 32 * j, k0, bb1, bb2);
-        if (blockIdx.x == 0 && blockIdx.y == 0 && blockIdx.z == 0) g_gemm_tc_dbg[0] = it + 1;
+        if (first_cta) g_gemm_tc_dbg[0] = it + 1;
       }
     }
   } else if (warp == 1) {
     // --------------------------------------------------------------- MMA --
     if (lane == 0) {
-      // kind::tf32 instruction descriptor: D f32, A/B tf32, majors, N>>3, M>>4
-      // (both operands are K-major in shared memory after the split pass)
-      uint32_t idesc = (1u << 4) | (2u << 7) | (2u << 10) | ((uint32_t)(TC_BN >> 3) << 17) |
-                       ((uint32_t)(TC_BM >> 4) << 24);
+      // kind::tf32 instruction descriptor: D f32, A/B tf32, K-major, N>>3, M>>4
+      const uint32_t idesc = (1u << 4) | (2u << 7) | (2u << 10) | ((uint32_t)(TC_BN >> 3) << 17) |
+                             ((uint32_t)(TC_BM >> 4) << 24);
       for (int it = 0; it < nk && ok; ++it) {
         const int s = it % TC_STAGES;
         const uint32_t ph = (uint32_t)(it / TC_STAGES) & 1u;
+        const int chunk = it / TC_CHUNK, acc = chunk & 1;
+        const bool chunk_start = (it % TC_CHUNK) == 0;
+        if (chunk_start && chunk >= 2 && !mbar_wait(&dempty[acc], (uint32_t)((chunk - 2) >> 1) & 1u, 5)) {
+          ok = false; break;
+        }
         if (!mbar_wait(&conv[s], ph, 2)) { ok = false; break; }
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
         const uint32_t base = smem_u32(smem + s * TC_STAGE_BYTES);
         const uint32_t a_hi = base, b_hi = base + TC_TILE_BYTES;
         const uint32_t a_lo = base + 2 * TC_TILE_BYTES, b_lo = base + 3 * TC_TILE_BYTES;
+        const uint32_t dacc = tmem + (uint32_t)(acc * TC_BN);
 #pragma unroll
         for (int kk = 0; kk < TC_BK / 8; ++kk) {
           // K-major tiles: 128 rows of 128 bytes (32 K values), 8-row groups
@@ -215,140 +281,100 @@ __global__ void __launch_bounds__(192, 1) gemm_tc_kernel(const __grid_constant__
           const uint32_t off = kk * 32;
           uint64_t dAh = umma_desc(a_hi + off, 16, 1024), dAl = umma_desc(a_lo + off, 16, 1024);
           uint64_t dBh = umma_desc(b_hi + off, 16, 1024), dBl = umma_desc(b_lo + off, 16, 1024);
-          const uint32_t first = (it == 0 && kk == 0 && P.dbg != 1) ? 0u : 1u;
-          umma_tf32(tmem, dAl, dBh, idesc, first);
-          umma_tf32(tmem, dAh, dBl, idesc, 1u);
-          umma_tf32(tmem, dAh, dBh, idesc, 1u);
+          const uint32_t first = (chunk_start && kk == 0) ? 0u : 1u;
+          umma_tf32(dacc, dAl, dBh, idesc, first);
+          umma_tf32(dacc, dAh, dBl, idesc, 1u);
+          umma_tf32(dacc, dAh, dBh, idesc, 1u);
         }
         umma_commit(&empty[s]);  // frees the stage once these MMAs have read it
-        if (blockIdx.x == 0 && blockIdx.y == 0 && blockIdx.z == 0) g_gemm_tc_dbg[2] = it + 1;
+        if ((it % TC_CHUNK) == TC_CHUNK - 1 || it == nk - 1) umma_commit(&dfull[acc]);
+        if (first_cta) g_gemm_tc_dbg[2] = it + 1;
       }
-      if (ok) umma_commit(accb);
     }
   } else {
-    // ------------------------------------------------ split, then epilogue --
+    // ---------------------------------------- split, drain, then epilogue --
     const int t = threadIdx.x - 64;  // 0..127
+    const int g = warp & 3;          // TMEM lane group this warp may access
+    float sum[TC_BN];
+#pragma unroll
+    for (int j = 0; j < TC_BN; ++j) sum[j] = 0.f;
+    int drained = 0;
+    auto drain = [&](int c) -> bool {
+      const int acc = c & 1;
+      if (!mbar_wait(&dfull[acc], (uint32_t)(c >> 1) & 1u, 4)) return false;
+      asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+#pragma unroll
+      for (int q = 0; q < TC_BN / 32; ++q) {
+        uint32_t r[32];
+        tmem_ld32(tmem + ((uint32_t)(g * 32) << 16) + (uint32_t)(acc * TC_BN + q * 32), r);
+        asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+        for (int j = 0; j < 32; ++j) sum[q * 32 + j] += __uint_as_float(r[j]);
+      }
+      asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+      mbar_arrive(&dempty[acc]);
+      return true;
+    };
     for (int it = 0; it < nk && ok; ++it) {
       const int s = it % TC_STAGES;
       const uint32_t ph = (uint32_t)(it / TC_STAGES) & 1u;
       if (!mbar_wait(&full[s], ph, 3)) { ok = false; break; }
       uint8_t* st = smem + s * TC_STAGE_BYTES;
-#pragma unroll 1
-      for (int op = 0; op < 2; ++op) {
-        const bool kmaj = op == 0 ? P.a_kmajor : P.b_kmajor;
-        uint8_t* hi_t = st + op * TC_TILE_BYTES;
-        uint8_t* lo_t = st + (2 + op) * TC_TILE_BYTES;
-        if (kmaj) {
-          // landed K-major: split in place, lo into the twin buffer (same layout)
-          float4* hi = reinterpret_cast<float4*>(hi_t);
-          float4* lo = reinterpret_cast<float4*>(lo_t);
-#pragma unroll 4
-          for (int q = t; q < TC_TILE_BYTES / 16; q += 128) {
-            float4 x = hi[q], h, l;
-            const float* xv = &x.x;
-            float* hv = &h.x;
-            float* lv = &l.x;
-#pragma unroll
-            for (int e = 0; e < 4; ++e) {
-              float hh = __uint_as_float(__float_as_uint(xv[e]) & 0xFFFFE000u);
-              hv[e] = hh;
-              lv[e] = xv[e] - hh;
-            }
-            hi[q] = h;
-            lo[q] = l;
-          }
-        } else {
-          // landed MN-major in staging: 4 boxes (MN chunk j) of 32 K-rows x
-          // 128 bytes; element (k, mn) sits in row k, 16-byte chunk
-          // (mn%32)/4 XOR (k%8). Write hi/lo transposed into the K-major
-          // tiles: element (mn, k) in row mn, chunk (k/4) XOR (mn%8).
-          const uint8_t* stg = st + (4 + op) * TC_TILE_BYTES;
-#pragma unroll 2
-          for (int q = t; q < TC_TILE_BYTES / 16; q += 128) {
-            const int j = q >> 8;          // MN chunk (256 float4 per 4 KB box)
-            const int k = (q >> 3) & 31;   // K row inside the box
-            const int pc = q & 7;          // physical 16-byte chunk
-            const int lc = pc ^ (k & 7);   // logical chunk -> mn = 4*lc .. 4*lc+3
-            const float4 x = *reinterpret_cast<const float4*>(stg + q * 16);
-            const float* xv = &x.x;
-#pragma unroll
-            for (int e = 0; e < 4; ++e) {
-              const int mn = j * 32 + lc * 4 + e;
-              const uint32_t o = (uint32_t)mn * 128u + (uint32_t)((((k >> 2) ^ (mn & 7)) << 4) + ((k & 3) << 2));
-              const float hh = __uint_as_float(__float_as_uint(xv[e]) & 0xFFFFE000u);
-              *reinterpret_cast<float*>(hi_t + o) = hh;
-              *reinterpret_cast<float*>(lo_t + o) = xv[e] - hh;
-            }
-          }
-        }
-      }
+      split_stage(st, t, P.a_kmajor, P.b_kmajor);
       asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
       mbar_arrive(&conv[s]);
-      if (t == 0 && blockIdx.x == 0 && blockIdx.y == 0 && blockIdx.z == 0) {
-        g_gemm_tc_dbg[1] = it + 1;
-        if (it == 0) {
-          g_gemm_tc_dbg[5] = __float_as_int(reinterpret_cast<float*>(st)[0]);  // A_hi (0,0)
-          g_gemm_tc_dbg[6] = __float_as_int(reinterpret_cast<float*>(st + TC_TILE_BYTES)[0]);
-        }
+      if (t == 0 && first_cta) g_gemm_tc_dbg[1] = it + 1;
+      // after splitting the last stage of chunk c+1, drain chunk c
+      if ((it % TC_CHUNK) == TC_CHUNK - 1 && it / TC_CHUNK >= 1) {
+        if (!drain(drained)) { ok = false; break; }
+        ++drained;
       }
     }
-    if (ok && mbar_wait(accb, 0, 4)) {
-      asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-      if (t == 0 && blockIdx.x == 0 && blockIdx.y == 0 && blockIdx.z == 0) {
-        g_gemm_tc_dbg[3] = 1;
-        g_gemm_tc_dbg[4] = (int)tmem;
-      }
-      const int g = warp & 3;  // TMEM lane group this warp may access
+    while (ok && drained < nchunks) {
+      if (!drain(drained)) { ok = false; break; }
+      ++drained;
+    }
+    if (ok) {
+      if (t == 0 && first_cta) g_gemm_tc_dbg[3] = 1;
       const int64_t row = m0 + g * 32 + lane;
       float* C = P.C + (int64_t)i1 * P.c_batch + (int64_t)i2 * P.c_batch2;
-#pragma unroll 1
-      for (int c = 0; c < TC_BN / 32; ++c) {
-        uint32_t r[32];
-        const uint32_t taddr = tmem + ((uint32_t)(g * 32) << 16) + (uint32_t)(c * 32);
-        asm volatile(
-            "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
-            "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
-            : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
-              "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]),
-              "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]),
-              "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]),
-              "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
-            : "r"(taddr));
-        asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-        if (c == 0 && t == 0 && blockIdx.x == 0 && blockIdx.y == 0 && blockIdx.z == 0) g_gemm_tc_dbg[7] = (int)r[0];
-        if (row >= P.M) continue;
-        const int64_t col0 = n0 + c * 32;
-        float* dst = C + row * P.ldc + col0;
-        const bool full_vec = (col0 + 32 <= P.N) && ((P.ldc & 3) == 0) && ((reinterpret_cast<uintptr_t>(dst) & 15) == 0);
-        if (full_vec) {
+      if (row < P.M) {
 #pragma unroll
-          for (int j = 0; j < 32; j += 4) {
-            float4 v = make_float4(__uint_as_float(r[j]), __uint_as_float(r[j + 1]), __uint_as_float(r[j + 2]),
-                                   __uint_as_float(r[j + 3]));
-            v.x *= P.alpha; v.y *= P.alpha; v.z *= P.alpha; v.w *= P.alpha;
-            if (P.bias) {
-              v.x += P.bias[col0 + j]; v.y += P.bias[col0 + j + 1];
-              v.z += P.bias[col0 + j + 2]; v.w += P.bias[col0 + j + 3];
-            }
-            float4* d4 = reinterpret_cast<float4*>(dst + j);
-            if (P.accumulate) {
-              float4 o = *d4;
-              v.x += o.x; v.y += o.y; v.z += o.z; v.w += o.w;
-            }
-            *d4 = v;
-          }
-        } else {
+        for (int q = 0; q < TC_BN / 32; ++q) {
+          const int64_t col0 = n0 + q * 32;
+          if (col0 >= P.N) break;
+          float* dst = C + row * P.ldc + col0;
+          const bool vec = (col0 + 32 <= P.N) && ((P.ldc & 3) == 0) &&
+                           ((reinterpret_cast<uintptr_t>(dst) & 15) == 0);
+          if (vec) {
 #pragma unroll
-          for (int j = 0; j < 32; ++j) {
-            if (col0 + j >= P.N) break;
-            float v = __uint_as_float(r[j]) * P.alpha;
-            if (P.bias) v += P.bias[col0 + j];
-            if (P.accumulate) v += dst[j];
-            dst[j] = v;
+            for (int j = 0; j < 32; j += 4) {
+              float4 v = make_float4(sum[q * 32 + j] * P.alpha, sum[q * 32 + j + 1] * P.alpha,
+                                     sum[q * 32 + j + 2] * P.alpha, sum[q * 32 + j + 3] * P.alpha);
+              if (P.bias) {
+                v.x += P.bias[col0 + j]; v.y += P.bias[col0 + j + 1];
+                v.z += P.bias[col0 + j + 2]; v.w += P.bias[col0 + j + 3];
+              }
+              float4* d4 = reinterpret_cast<float4*>(dst + j);
+              if (P.accumulate) {
+                float4 o = *d4;
+                v.x += o.x; v.y += o.y; v.z += o.z; v.w += o.w;
+              }
+              *d4 = v;
+            }
+          } else {
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
+              if (col0 + j < P.N) {
+                float v = sum[q * 32 + j] * P.alpha;
+                if (P.bias) v += P.bias[col0 + j];
+                if (P.accumulate) v += dst[j];
+                dst[j] = v;
+              }
+            }
           }
         }
       }
-      asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
     }
   }
   __syncthreads();
@@ -441,10 +467,7 @@ bool launch_gemm_tc(const GemmDesc& g, cudaStream_t s) {
   p.b_b1 = g.b_batch ? 1 : 0; p.b_b2 = g.b_batch2 ? 1 : 0;
   p.C = g.C; p.ldc = g.ldc; p.c_batch = g.c_batch; p.c_batch2 = g.c_batch2;
   p.bias = g.bias; p.alpha = g.alpha; p.accumulate = g.accumulate;
-  {
-    const char* d = getenv("TG_GEMM_TC_DEBUG");
-    p.dbg = d ? atoi(d) : 0;
-  }
+
   static bool attr = false;
   if (!attr) {
     if (cudaFuncSetAttribute(gemm_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, TC_SMEM) != cudaSuccess)
