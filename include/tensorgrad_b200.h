@@ -104,6 +104,20 @@ int tg_debug_gemm_error(int reset);
 /* Progress markers of the first GEMM tile (8 ints) for pipeline diagnosis. */
 int tg_debug_gemm_dbg(int* out8);
 
+/* Column sums of a row-major [outer, inner] f32 matrix already on the device
+ * (out[j] = sum_i x[i*inner + j]), enqueued on `stream` (a cudaStream_t; NULL
+ * for the legacy default stream), without allocating anything. It has no
+ * counterpart in the reference: it serves callers that may not allocate
+ * device memory, such as a host whose pool or caching allocator owns all of
+ * the GPU's memory, or a latency-critical loop that must not call cudaMalloc
+ * because it can synchronize the device. The deterministic two-pass kernel's
+ * partial sums live in a fixed 256 Ki-float (1 MiB) device array that every
+ * GPU loading the library holds until exit; shapes that need more partial
+ * sums than that are rejected with an error. The first call on each device
+ * looks up the array's address and should come before any stream capture.
+ * All calls share the array: calls that overlap on the GPU race. */
+int tg_colsum_noalloc(const float* x, float* out, int64_t outer, int64_t inner, void* stream);
+
 const char* tg_last_error_name(void);
 const char* tg_last_error_message(void);
 

@@ -58,6 +58,15 @@ void write_str(const std::string& s, char* buf, size_t cap, size_t* needed) {
 }
 }  // namespace
 
+namespace tg {
+int api_fail(const std::string& name, const std::string& msg) { return fail(name, msg); }
+int api_ok() {
+  g_err_name.clear();
+  g_err_msg.clear();
+  return TG_OK;
+}
+}  // namespace tg
+
 extern "C" {
 
 int tg_nccl_unique_id(uint8_t out[128]) {
