@@ -231,7 +231,8 @@ def main():
     ms, e2e_ms = float(ms_t[0]), float(ms_t[1])
 
     # per-launch profile (outside the timed region)
-    kinds = dg.launch_list()
+    labels = dg.launch_list()
+    kinds = [x.split("|")[0] for x in labels]
     prof = dg.profile_step()
     by_kind = {}
     for k, t in zip(kinds, prof):

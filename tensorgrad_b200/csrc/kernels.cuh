@@ -132,7 +132,13 @@ struct GemmDesc {
   int accumulate;                                 // C += result
   int64_t batch2;                                 // inner batch extent (1 = single batch dim)
   int64_t a_batch2, b_batch2, c_batch2;           // strides of the inner batch index
+  float* workspace;                               // split-K partial tiles (may be null)
+  int64_t workspace_floats;
 };
+// K-splits the tensor-core GEMM would use for this problem (1 = none) and the
+// workspace floats that needs.
+int gemm_tc_splits(int64_t M, int64_t N, int64_t K, int64_t batch);
+int64_t gemm_tc_workspace_floats(int64_t M, int64_t N, int64_t K, int64_t batch);
 void launch_gemm_simt(const GemmDesc& g, cudaStream_t s);
 // tcgen05/TMEM 3xTF32 GEMM; returns false when the shape/layout is not taken.
 bool launch_gemm_tc(const GemmDesc& g, cudaStream_t s);

@@ -60,6 +60,8 @@ struct TcParams {
   const float* bias;
   float alpha;
   int accumulate;
+  int splits, kps;  // split-K: number of K ranges and K-stages per range
+  float* ws;        // [splits][batch][M][N] partial tiles when splits > 1
 };
 
 // ------------------------------------------------------------- PTX helpers --
@@ -205,11 +207,15 @@ __global__ void __launch_bounds__(192, 1) gemm_tc_kernel(const __grid_constant__
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int64_t n0 = (int64_t)blockIdx.x * TC_BN, m0 = (int64_t)blockIdx.y * TC_BM;
-  const int64_t z = blockIdx.z;
-  const int i1 = (int)(z / P.batch2), i2 = (int)(z % P.batch2);
-  const int nk = (int)((P.K + TC_BK - 1) / TC_BK);
+  const int64_t zb = blockIdx.z / P.splits;   // batch index
+  const int sp = blockIdx.z % P.splits;       // K range
+  const int i1 = (int)(zb / P.batch2), i2 = (int)(zb % P.batch2);
+  const int nk_all = (int)((P.K + TC_BK - 1) / TC_BK);
+  const int kbeg = sp * P.kps;
+  const int nk = max(0, min(nk_all, kbeg + P.kps) - kbeg);
   const int nchunks = (nk + TC_CHUNK - 1) / TC_CHUNK;
   const bool first_cta = blockIdx.x == 0 && blockIdx.y == 0 && blockIdx.z == 0;
+  const bool partial = P.splits > 1;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < TC_STAGES; ++s) {
@@ -244,7 +250,7 @@ __global__ void __launch_bounds__(192, 1) gemm_tc_kernel(const __grid_constant__
         if (it >= TC_STAGES && !mbar_wait(&empty[s], ph ^ 1u, 1)) { ok = false; break; }
         uint8_t* st = smem + s * TC_STAGE_BYTES;
         mbar_expect_tx(&full[s], 2 * TC_TILE_BYTES);
-        const int k0 = it * TC_BK;
+        const int k0 = (kbeg + it) * TC_BK;
         if (P.a_kmajor) tma_load_4d(&tmA, &full[s], st, k0, (int)m0, ab1, ab2);
         else for (int j = 0; j < 4; ++j)
           tma_load_4d(&tmA, &full[s], st + 4 * TC_TILE_BYTES + j * 4096, (int)m0 + 32 * j, k0, ab1, ab2);
@@ -337,26 +343,32 @@ __global__ void __launch_bounds__(192, 1) gemm_tc_kernel(const __grid_constant__
     if (ok) {
       if (t == 0 && first_cta) g_gemm_tc_dbg[3] = 1;
       const int64_t row = m0 + g * 32 + lane;
-      float* C = P.C + (int64_t)i1 * P.c_batch + (int64_t)i2 * P.c_batch2;
+      // split-K: raw partial tile into the workspace, finished by gemm_splitk_reduce
+      float* C = partial ? P.ws + ((int64_t)sp * P.batch + zb) * P.M * P.N
+                         : P.C + (int64_t)i1 * P.c_batch + (int64_t)i2 * P.c_batch2;
+      const int64_t ldc = partial ? P.N : P.ldc;
+      const float alpha = partial ? 1.f : P.alpha;
+      const float* bias = partial ? nullptr : P.bias;
+      const int accumulate = partial ? 0 : P.accumulate;
       if (row < P.M) {
 #pragma unroll
         for (int q = 0; q < TC_BN / 32; ++q) {
           const int64_t col0 = n0 + q * 32;
           if (col0 >= P.N) break;
-          float* dst = C + row * P.ldc + col0;
-          const bool vec = (col0 + 32 <= P.N) && ((P.ldc & 3) == 0) &&
+          float* dst = C + row * ldc + col0;
+          const bool vec = (col0 + 32 <= P.N) && ((ldc & 3) == 0) &&
                            ((reinterpret_cast<uintptr_t>(dst) & 15) == 0);
           if (vec) {
 #pragma unroll
             for (int j = 0; j < 32; j += 4) {
-              float4 v = make_float4(sum[q * 32 + j] * P.alpha, sum[q * 32 + j + 1] * P.alpha,
-                                     sum[q * 32 + j + 2] * P.alpha, sum[q * 32 + j + 3] * P.alpha);
-              if (P.bias) {
-                v.x += P.bias[col0 + j]; v.y += P.bias[col0 + j + 1];
-                v.z += P.bias[col0 + j + 2]; v.w += P.bias[col0 + j + 3];
+              float4 v = make_float4(sum[q * 32 + j] * alpha, sum[q * 32 + j + 1] * alpha,
+                                     sum[q * 32 + j + 2] * alpha, sum[q * 32 + j + 3] * alpha);
+              if (bias) {
+                v.x += bias[col0 + j]; v.y += bias[col0 + j + 1];
+                v.z += bias[col0 + j + 2]; v.w += bias[col0 + j + 3];
               }
               float4* d4 = reinterpret_cast<float4*>(dst + j);
-              if (P.accumulate) {
+              if (accumulate) {
                 float4 o = *d4;
                 v.x += o.x; v.y += o.y; v.z += o.z; v.w += o.w;
               }
@@ -366,9 +378,9 @@ __global__ void __launch_bounds__(192, 1) gemm_tc_kernel(const __grid_constant__
 #pragma unroll
             for (int j = 0; j < 32; ++j) {
               if (col0 + j < P.N) {
-                float v = sum[q * 32 + j] * P.alpha;
-                if (P.bias) v += P.bias[col0 + j];
-                if (P.accumulate) v += dst[j];
+                float v = sum[q * 32 + j] * alpha;
+                if (bias) v += bias[col0 + j];
+                if (accumulate) v += dst[j];
                 dst[j] = v;
               }
             }
@@ -381,6 +393,24 @@ __global__ void __launch_bounds__(192, 1) gemm_tc_kernel(const __grid_constant__
   if (warp == 1) {
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TC_TMEM_COLS));
+  }
+}
+
+// Deterministic split-K reduction: C = alpha * sum_sp ws[sp] (+bias) (+C),
+// summed in split order.
+__global__ void __launch_bounds__(256) gemm_splitk_reduce(const __grid_constant__ TcParams P) {
+  const int64_t per = P.M * P.N;
+  const int64_t total = per * P.batch;
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < total; e += stride) {
+    const int64_t zb = e / per, rem = e % per, row = rem / P.N, col = rem % P.N;
+    float v = 0.f;
+    for (int sp = 0; sp < P.splits; ++sp) v += P.ws[(int64_t)sp * total + e];
+    v *= P.alpha;
+    if (P.bias) v += P.bias[col];
+    const int64_t i1 = zb / P.batch2, i2 = zb % P.batch2;
+    float* d = P.C + i1 * P.c_batch + i2 * P.c_batch2 + row * P.ldc + col;
+    *d = P.accumulate ? *d + v : v;
   }
 }
 
@@ -430,6 +460,22 @@ static bool make_map(CUtensorMap* tm, const float* base, bool kmajor, int64_t mn
   return r == CUDA_SUCCESS;
 }
 
+int gemm_tc_splits(int64_t M, int64_t N, int64_t K, int64_t batch) {
+  const int64_t tiles = ((M + TC_BM - 1) / TC_BM) * ((N + TC_BN - 1) / TC_BN) * batch;
+  const int64_t nk = (K + TC_BK - 1) / TC_BK;
+  const int64_t sms = device_sm_count();
+  if (tiles >= sms || nk < 16) return 1;
+  int64_t s = (2 * sms) / tiles;        // about two CTAs per SM
+  s = s < nk / 8 ? s : nk / 8;          // at least 8 K-stages per split
+  s = s < 32 ? s : 32;
+  return s < 2 ? 1 : (int)s;
+}
+
+int64_t gemm_tc_workspace_floats(int64_t M, int64_t N, int64_t K, int64_t batch) {
+  const int s = gemm_tc_splits(M, N, K, batch);
+  return s > 1 ? (int64_t)s * batch * M * N : 0;
+}
+
 static bool tc_enabled() {
   static int v = -1;
   if (v < 0) {
@@ -467,6 +513,13 @@ bool launch_gemm_tc(const GemmDesc& g, cudaStream_t s) {
   p.b_b1 = g.b_batch ? 1 : 0; p.b_b2 = g.b_batch2 ? 1 : 0;
   p.C = g.C; p.ldc = g.ldc; p.c_batch = g.c_batch; p.c_batch2 = g.c_batch2;
   p.bias = g.bias; p.alpha = g.alpha; p.accumulate = g.accumulate;
+  const int64_t nk = (g.K + TC_BK - 1) / TC_BK;
+  int splits = gemm_tc_splits(g.M, g.N, g.K, g.batch);
+  if (splits > 1 && (!g.workspace || g.workspace_floats < (int64_t)splits * g.batch * g.M * g.N)) splits = 1;
+  p.kps = (int)((nk + splits - 1) / splits);
+  splits = (int)((nk + p.kps - 1) / p.kps);  // every split gets at least one K-stage
+  p.splits = splits;
+  p.ws = g.workspace;
 
   static bool attr = false;
   if (!attr) {
@@ -474,8 +527,14 @@ bool launch_gemm_tc(const GemmDesc& g, cudaStream_t s) {
       return false;
     attr = true;
   }
-  dim3 grid((unsigned)((g.N + TC_BN - 1) / TC_BN), (unsigned)((g.M + TC_BM - 1) / TC_BM), (unsigned)g.batch);
+  dim3 grid((unsigned)((g.N + TC_BN - 1) / TC_BN), (unsigned)((g.M + TC_BM - 1) / TC_BM),
+            (unsigned)(g.batch * splits));
   gemm_tc_kernel<<<grid, 192, TC_SMEM, s>>>(ta, tb, p);
+  if (splits > 1) {
+    int64_t total = g.batch * g.M * g.N;
+    int64_t blocks = (total + 255) / 256, cap = (int64_t)device_sm_count() * 8;
+    gemm_splitk_reduce<<<(unsigned)(blocks < cap ? blocks : cap), 256, 0, s>>>(p);
+  }
   return true;
 }
 

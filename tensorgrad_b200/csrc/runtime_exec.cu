@@ -130,6 +130,14 @@ static int64_t scratch_for(const Program& P, int i, int action) {
     int64_t D = P.T[a].shape.back();
     return (int64_t)row_scratch_floats(k == "sum_last" ? ROW_SUM : ROW_MEAN, P.T[a].numel / std::max<int64_t>(D, 1), D) * 4;
   }
+  if (k == "matmul" || k == "matmul_batched") {
+    const auto& os = P.T[P.out[i]].shape;
+    int a = P.op(i)["a"].i32();
+    int64_t K = P.T[a].shape.back(), N = os.back(), M = os[os.size() - 2], batch = 1;
+    for (size_t d = 0; d + 2 < os.size(); ++d) batch *= os[d];
+    // either the batch folds into M (matmul) or stays a batch: same M*N*batch
+    return 4 * std::max(gemm_tc_workspace_floats(M * batch, N, K, 1), gemm_tc_workspace_floats(M, N, K, batch));
+  }
   if (k == "sum_to_shape") {
     int a = P.op(i)["a"].i32();
     int64_t inner = P.T[P.out[i]].numel;
@@ -703,7 +711,13 @@ void Graph::emit_launches() {
         g.a_batch = SA[0]; g.b_batch = SB[0]; g.c_batch = SC[0];
         g.a_batch2 = SA[1]; g.b_batch2 = SB[1]; g.c_batch2 = SC[1];
       }
-      add(k, [g](cudaStream_t s) { if (!launch_gemm_tc(g, s)) launch_gemm_simt(g, s); });
+      g.workspace = scratch;
+      g.workspace_floats = (int64_t)scratch_floats;
+      char label[160];
+      snprintf(label, sizeof label, "%s|M=%lld N=%lld K=%lld b=%lld A%s B%s", k.c_str(), (long long)g.M,
+               (long long)g.N, (long long)g.K, (long long)g.batch, g.lda_k == 1 ? "k" : "mn",
+               g.ldb_k == 1 ? "k" : "mn");
+      add(label, [g](cudaStream_t s) { if (!launch_gemm_tc(g, s)) launch_gemm_simt(g, s); });
       continue;
     }
     // ---------------------------------------------------------- layout --

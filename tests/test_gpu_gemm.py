@@ -49,3 +49,11 @@ def test_gemm_tc_error_flag_clear(ctx):
     from tensorgrad_b200 import backend as BK
     lib = BK.load()
     assert lib.tg_debug_gemm_error(1) == 0
+
+
+def test_gemm_split_k_batched(ctx):
+    """Few output tiles and a long K: the K range is split over CTAs and the
+    partial tiles are summed in split order."""
+    a = rnd([3, 64, 2048], 46)
+    b = rnd([3, 2048, 96], 47)
+    run(ctx, lambda: tg.matmul(T("a", [3, 64, 2048]), T("b", [3, 2048, 96])), {"a": a, "b": b})
