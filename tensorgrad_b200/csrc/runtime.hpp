@@ -7,6 +7,8 @@
 // and a mapAsync per step) and its WGSL codegen (src/codegen.ts:48-56).
 #pragma once
 #include <cuda_runtime.h>
+#include <cstdio>
+#include <cstdlib>
 #include <functional>
 #include <map>
 #include <memory>
@@ -46,6 +48,25 @@ struct Writeback {
 
 // Parsed wire program. Field names mirror the reference's graph + BufferPlan
 // vocabulary (src/ir.ts:284-296, src/buffers.ts:61-80).
+// f32 of the decimal string x.toFixed(8): how the reference writes a float
+// literal into its shader source (dropout p and scale).
+inline float f32_lit8(double x) {
+  char buf[64];
+  snprintf(buf, sizeof buf, "%.8f", x);
+  return (float)strtod(buf, nullptr);
+}
+
+// A kernel generated at plan time and compiled with NVRTC (jit.cu).
+struct JitFn {
+  std::string name, src;
+  int device = 0;
+  void* fn = nullptr;  // CUfunction, set by jit_compile_pending
+};
+std::shared_ptr<JitFn> jit_request(const std::string& name, const std::string& src);
+void jit_compile_pending();
+void jit_launch(const JitFn& f, unsigned grid, unsigned block, void** args, cudaStream_t s);
+const std::string& jit_preamble();
+
 struct Program {
   tgjson::Value root;
   std::vector<TInfo> T;
@@ -133,7 +154,13 @@ class Graph {
   void plan_views();
   void plan_optimizer();
   void plan_storage();
+  void plan_fusion();
   void emit_launches();
+  EwInput ew_input(int t, const std::vector<int64_t>& oshape, bool& vec_ok);
+  void emit_ew_group(int root, const int* seed_ptr,
+                     const std::function<void(const std::string&, std::function<void(cudaStream_t)>)>& add);
+  int ew_pos(int i) const { return ew_root_.empty() || ew_root_[i] < 0 ? i : ew_root_[i]; }
+  bool ew_internal(int t) const;
   void run_launches(cudaStream_t s);
   void init_constants();
   void* ptr(int t) const;
@@ -145,6 +172,8 @@ class Graph {
   std::vector<int> action_;          // per op: planned action code
   std::vector<StorageLoc> loc_;      // per root tensor
   std::vector<int> op_done_;         // ops folded away
+  std::vector<int> ew_root_;         // per op: root op of its fused elementwise group, or -1
+  bool jit_ = false;                 // fused elementwise groups compiled at plan time
   void* arena_[AR_COUNT] = {};
   int64_t arena_bytes_[AR_COUNT] = {};
   bool arena_owned_[AR_COUNT] = {};

@@ -18,11 +18,6 @@ static std::vector<int64_t> cstrides(const std::vector<int64_t>& shape) {
   return s;
 }
 static int64_t align256(int64_t b) { return (b + 255) / 256 * 256; }
-static float f32_lit8(double x) {
-  char buf[64];
-  snprintf(buf, sizeof buf, "%.8f", x);
-  return (float)strtod(buf, nullptr);
-}
 static bool is_leaf_kind(const std::string& k) {
   return k == "param_input" || k == "tensor_input" || k == "state_input";
 }
@@ -86,6 +81,7 @@ void Graph::plan() {
   if (ctx->world > 1 && !parent && P.optimizer && !adam_fused_ && !sgd_fused_)
     throw TgError("Error", "data-parallel training needs the fused optimizer path; this optimizer graph "
                            "does not match the Adam/AdamW/SGD update patterns");
+  plan_fusion();
   plan_storage();
   init_constants();
   emit_launches();
@@ -166,7 +162,10 @@ void Graph::plan_storage() {
   for (int i = 0; i < nO; ++i) {
     if (op_done_[i]) continue;
     int o = P.out[i];
-    if (views_[o].root == o) { used[o] = 1; if (def[o] < 0) def[o] = i; end[o] = std::max(end[o], i); }
+    // A fused elementwise group runs at its root op: its members' operands are
+    // read there, and values passed inside the group need no storage.
+    const int pos = ew_pos(i);
+    if (views_[o].root == o && !ew_internal(o)) { used[o] = 1; if (def[o] < 0) def[o] = i; end[o] = std::max(end[o], i); }
     if (action_[i] == 100 || action_[i] == 101) {
       int a = P.op(i)["a"].i32();
       int oh = action_[i] == 100 ? a : P.op(P.producer[P.op(P.producer[a])["a"].i32()])["a"].i32();
@@ -175,7 +174,8 @@ void Graph::plan_storage() {
       touch(P.op(i)["b"].i32(), i);
       continue;
     }
-    for (int t : P.op_inputs[i]) touch(t, i);
+    for (int t : P.op_inputs[i])
+      if (!ew_internal(t)) touch(t, pos);
   }
   for (int t : pinned) used[t] = 1;
   if (P.loss >= 0) { pinned.insert(views_[P.loss].root); used[views_[P.loss].root] = 1; }
@@ -365,6 +365,58 @@ struct EwBuilder {
 
 static bool aligned16(const void* p) { return ((uintptr_t)p & 15) == 0; }
 
+EwInput Graph::ew_input(int t, const std::vector<int64_t>& oshape, bool& vec_ok) {
+  EwInput in{};
+  const TView& v = views_[t];
+  const auto& ts = P.T[t].shape;
+  in.dtype = P.T[t].dtype;
+  int R = (int)oshape.size(), rd = R - (int)ts.size();
+  if (v.onehot) {
+    if (ts != oshape) throw TgError("Error", "internal: virtual one-hot read with broadcast");
+    in.mode = IN_ONEHOT;
+    in.ptr = ptr(v.onehot_idx);
+    in.period = ts.back();
+    return in;
+  }
+  in.ptr = ptr(t);
+  if (P.T[t].numel == 1) { in.mode = IN_SCALAR; return in; }
+  std::vector<int64_t> pt(R, 1);
+  for (size_t i = 0; i < ts.size(); ++i) pt[rd + i] = ts[i];
+  if (v.contiguous) {
+    if (pt == oshape) { in.mode = IN_FULL; if (!aligned16(in.ptr)) vec_ok = false; return in; }
+    // suffix broadcast
+    int k = 0;
+    while (k < R && pt[k] == 1) ++k;
+    bool suffix = true;
+    for (int i = k; i < R; ++i) if (pt[i] != oshape[i]) suffix = false;
+    if (suffix) {
+      in.mode = IN_PERIOD; in.period = P.T[t].numel;
+      if (in.period % 4 || !aligned16(in.ptr)) vec_ok = false;
+      return in;
+    }
+    // prefix (trailing size-1 axes)
+    int j = R;
+    while (j > 0 && pt[j - 1] == 1) --j;
+    bool prefix = true;
+    for (int i = 0; i < j; ++i) if (pt[i] != oshape[i]) prefix = false;
+    if (prefix) {
+      int64_t per = 1;
+      for (int i = j; i < R; ++i) per *= oshape[i];
+      in.mode = IN_ROWDIV; in.period = per;
+      if (per % 4) vec_ok = false;
+      return in;
+    }
+  }
+  if (R > EW_MAX_RANK) throw TgError("Error", "elementwise op rank > 6 with a strided operand");
+  in.mode = IN_STRIDED;
+  for (int i = 0; i < R; ++i) {
+    if (i < rd) in.strides[i] = 0;
+    else in.strides[i] = (pt[i] == 1 && oshape[i] != 1) ? 0 : v.strides[i - rd];
+  }
+  vec_ok = false;
+  return in;
+}
+
 void Graph::emit_launches() {
   launches_.clear();
   launch_kind_.clear();
@@ -382,55 +434,7 @@ void Graph::emit_launches() {
   };
 
   auto mk_input = [&](int t, const std::vector<int64_t>& oshape, bool& vec_ok) -> EwInput {
-    EwInput in{};
-    const TView& v = views_[t];
-    const auto& ts = P.T[t].shape;
-    in.dtype = P.T[t].dtype;
-    int R = (int)oshape.size(), rd = R - (int)ts.size();
-    if (v.onehot) {
-      if (ts != oshape) throw TgError("Error", "internal: virtual one-hot read with broadcast");
-      in.mode = IN_ONEHOT;
-      in.ptr = ptr(v.onehot_idx);
-      in.period = ts.back();
-      return in;
-    }
-    in.ptr = ptr(t);
-    if (P.T[t].numel == 1) { in.mode = IN_SCALAR; return in; }
-    std::vector<int64_t> pt(R, 1);
-    for (size_t i = 0; i < ts.size(); ++i) pt[rd + i] = ts[i];
-    if (v.contiguous) {
-      if (pt == oshape) { in.mode = IN_FULL; if (!aligned16(in.ptr)) vec_ok = false; return in; }
-      // suffix broadcast
-      int k = 0;
-      while (k < R && pt[k] == 1) ++k;
-      bool suffix = true;
-      for (int i = k; i < R; ++i) if (pt[i] != oshape[i]) suffix = false;
-      if (suffix) {
-        in.mode = IN_PERIOD; in.period = P.T[t].numel;
-        if (in.period % 4 || !aligned16(in.ptr)) vec_ok = false;
-        return in;
-      }
-      // prefix (trailing size-1 axes)
-      int j = R;
-      while (j > 0 && pt[j - 1] == 1) --j;
-      bool prefix = true;
-      for (int i = 0; i < j; ++i) if (pt[i] != oshape[i]) prefix = false;
-      if (prefix) {
-        int64_t per = 1;
-        for (int i = j; i < R; ++i) per *= oshape[i];
-        in.mode = IN_ROWDIV; in.period = per;
-        if (per % 4) vec_ok = false;
-        return in;
-      }
-    }
-    if (R > EW_MAX_RANK) throw TgError("Error", "elementwise op rank > 6 with a strided operand");
-    in.mode = IN_STRIDED;
-    for (int i = 0; i < R; ++i) {
-      if (i < rd) in.strides[i] = 0;
-      else in.strides[i] = (pt[i] == 1 && oshape[i] != 1) ? 0 : v.strides[i - rd];
-    }
-    vec_ok = false;
-    return in;
+    return ew_input(t, oshape, vec_ok);
   };
 
   auto finish_ew = [&](EwBuilder& B, int out_t, int out_reg, bool vec_ok, const std::string& kind) {
@@ -514,6 +518,10 @@ void Graph::emit_launches() {
       continue;
     }
     // ---------------------------------------------------- elementwise --
+    if (jit_ && ew_root_[i] >= 0) {
+      if (ew_root_[i] == i) emit_ew_group(i, seed_ptr, add);
+      continue;
+    }
     static const std::map<std::string, int> bin = {{"add", EW_ADD}, {"sub", EW_SUB}, {"mul", EW_MUL},
                                                    {"div", EW_DIV}, {"min", EW_MIN}, {"max", EW_MAX}};
     static const std::map<std::string, int> un = {
@@ -882,6 +890,7 @@ void Graph::emit_launches() {
       launch_scale(la, 1, inv, s);
     });
   }
+  jit_compile_pending();
 }
 
 // ------------------------------------------------------------ execution --
