@@ -163,9 +163,12 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours")
     ap.add_argument("--config", default="c4")
+    ap.add_argument("--batch", type=int, default=None,
+                    help="sequences per GPU (default: the config's; smaller only for profiling captures)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--profile-out", default=None, help="write per-launch (label, ms) of one profiled step as JSON")
     args = ap.parse_args()
-    w = CF.workload(args.config)
+    w = CF.workload(args.config, **({"batch": args.batch} if args.batch else {}))
     if args.impl == "reference":
         return run_reference(args, w)
 
@@ -234,6 +237,9 @@ def main():
     labels = dg.launch_list()
     kinds = [x.split("|")[0] for x in labels]
     prof = dg.profile_step()
+    if args.profile_out and rank == 0:
+        with open(args.profile_out, "w") as f:
+            json.dump([[lab, t] for lab, t in zip(labels, prof)], f)
     by_kind = {}
     for k, t in zip(kinds, prof):
         by_kind[k] = by_kind.get(k, 0.0) + t

@@ -7,22 +7,32 @@
 // Accuracy: each f32 operand x is split into hi = x with the low 13 mantissa
 // bits cleared (exactly representable in TF32) and lo = x - hi (exact in
 // f32, then truncated to TF32 by the tensor core). The product is
-// accumulated as lo_a*hi_b + hi_a*lo_b + hi_a*hi_b in one f32 TMEM
-// accumulator; the dropped lo_a*lo_b term and the truncation of lo are
-// ~2^-20 relative, so results match an f32 GEMM to ~1e-6.
+// accumulated as lo_a*hi_b + hi_a*lo_b + hi_a*hi_b; the dropped lo_a*lo_b
+// term and the truncation of lo are ~2^-20 relative.
 //
-// Structure (one CTA per 128x128 output tile, 192 threads):
-//   warp 0     TMA producer: per 32-deep K stage loads the A and B tiles
-//              (128B-swizzled; K-major: one 128x32 box; MN-major: sixteen
-//              8(K)x32(MN) boxes in UMMA's canonical MN-major atom order)
-//              into a 3-stage ring
-//   warp 1     allocates TMEM (128 f32 columns), issues the tcgen05.mma
-//              instructions (M=128, N=128, K=8, kind::tf32) from one thread,
-//              commits each stage back to the producer
-//   warps 2-5  split each landed stage into K-major hi and lo tiles (in
-//              place for K-major operands; transposed out of a staging box for
-//              MN-major ones), drain finished accumulator chunks into f32
-//              registers, then store alpha*acc (+bias) (+C)
+// Data path. A tcgen05 MMA with M=128, N=128, K=8 reads 8 KB of operands in
+// 64 clocks when both come from shared memory, which is all of the SM's
+// shared-memory bandwidth; three of them per K step plus the split's own
+// traffic would leave the tensor pipe idle more than half the time. So only
+// B is a shared-memory operand. A goes through tensor memory: the split warps
+// read each A row once from the TMA-landed tile, and write its hi and lo
+// parts into TMEM with tcgen05.st, and the MMA takes A from TMEM. This also
+// makes A's layout free (a K-major or MN-major tile is just read row- or
+// column-wise). B must be K-major in shared memory for kind::tf32; the host
+// swaps the operands (C^T = B^T A^T) when that puts a K-major operand in B's
+// place, and only when neither operand is K-major (weight gradients: both
+// are [tokens, features]) do the split warps transpose B.
+//
+// Structure (one CTA per 128x128 output tile, 192 threads, 3-stage ring):
+//   warp 0     TMA producer: per 32-deep K stage, the A tile (K-major: one
+//              128x32 box; MN-major: four 32x32 boxes) and the B tile, all
+//              128B-swizzled
+//   warp 1     allocates all 512 TMEM columns (two 128-column accumulators,
+//              then 64 columns of A hi/lo per stage) and issues the MMAs from
+//              one thread, committing each stage back to the producer
+//   warps 2-5  per stage: A rows -> hi/lo in TMEM, B -> K-major hi/lo tiles
+//              in shared memory; drain finished accumulator chunks into f32
+//              registers; finally store alpha*acc (+bias) (+C)
 // Every mbarrier wait is bounded; on timeout the kernel records an error
 // code in g_gemm_tc_error and leaves without further waits.
 #include <cuda.h>
@@ -41,13 +51,15 @@ __device__ int g_gemm_tc_error = 0;
 // [3] epilogue reached.
 __device__ int g_gemm_tc_dbg[8];
 
-constexpr int TC_BM = 128, TC_BN = 128, TC_BK = 32, TC_STAGES = 2;
-constexpr int TC_TILE_BYTES = 128 * TC_BK * 4;           // 16 KB per operand tile
-// A_hi, B_hi, A_lo, B_lo (K-major, what the MMA reads) + A/B staging for
-// MN-major operands (what TMA writes when the operand is not K-major)
-constexpr int TC_STAGE_BYTES = 6 * TC_TILE_BYTES;
+constexpr int TC_BM = 128, TC_BN = 128, TC_BK = 32, TC_STAGES = 3;
+constexpr int TC_TILE_BYTES = 128 * TC_BK * 4;  // 16 KB per operand tile
+// Per stage: [0] A as landed by TMA, [1] B hi (K-major MMA operand; TMA lands
+// a K-major B here and it is split in place), [2] B lo, [3] B as landed when
+// it is MN-major.
+constexpr int TC_STAGE_BYTES = 4 * TC_TILE_BYTES;
 constexpr int TC_SMEM = TC_STAGES * TC_STAGE_BYTES + 1024 + 256;
-constexpr uint32_t TC_TMEM_COLS = 256;  // two 128-column accumulators
+constexpr uint32_t TC_TMEM_COLS = 512;
+constexpr uint32_t TC_ACOL = 2 * TC_BN;  // first TMEM column of the per-stage A hi/lo (64 columns each)
 constexpr long long TC_SPIN_LIMIT = 1ll << 22;
 
 struct TcParams {
@@ -56,8 +68,10 @@ struct TcParams {
   int a_kmajor, b_kmajor;
   int a_b1, a_b2, b_b1, b_b2;  // 1 when that operand varies with the batch index
   float* C;
-  int64_t ldc, c_batch, c_batch2;
+  int64_t c_m, c_n;            // C(m, n) at C[m*c_m + n*c_n] (c_m == 1 after an operand swap)
+  int64_t c_batch, c_batch2;
   const float* bias;
+  int bias_m;                  // bias indexed by m (after an operand swap) instead of n
   float alpha;
   int accumulate;
   int splits, kps;  // split-K: number of K ranges and K-stages per range
@@ -107,28 +121,20 @@ __device__ __forceinline__ uint64_t umma_desc(uint32_t saddr, uint32_t lbo, uint
   d |= (uint64_t)2 << 61;  // 128-byte swizzle
   return d;
 }
-__device__ __forceinline__ void umma_tf32(uint32_t tmem_d, uint64_t da, uint64_t db, uint32_t idesc, uint32_t acc) {
+// D (TMEM) (+)= A (TMEM) * B (shared memory descriptor), kind::tf32.
+__device__ __forceinline__ void umma_tf32_ts(uint32_t tmem_d, uint32_t tmem_a, uint64_t db, uint32_t idesc,
+                                             uint32_t acc) {
   // The disable-output-lane mask is given explicitly (all lanes enabled).
   const uint32_t z = 0;
   asm volatile(
       "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
-      " tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, {%5, %6, %7, %8}, p;\n}\n"
-      ::"r"(tmem_d), "l"(da), "l"(db), "r"(idesc), "r"(acc), "r"(z), "r"(z), "r"(z), "r"(z));
+      " tcgen05.mma.cta_group::1.kind::tf32 [%0], [%1], %2, %3, {%5, %6, %7, %8}, p;\n}\n"
+      ::"r"(tmem_d), "r"(tmem_a), "l"(db), "r"(idesc), "r"(acc), "r"(z), "r"(z), "r"(z), "r"(z));
 }
 __device__ __forceinline__ void umma_commit(uint64_t* bar) {
   asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
                : "memory");
 }
-
-// ------------------------------------------------------------------ kernel --
-// Accumulator chunking: the tensor core accumulates in f32 without
-// round-to-nearest on every add, so error grows with the number of
-// accumulation steps. The MMA warp therefore alternates between two TMEM
-// accumulators every TC_CHUNK K-stages (384 MMA-K), and the split/epilogue
-// warps drain each finished accumulator into per-thread f32 registers with
-// round-to-nearest adds; total error then grows like sqrt(K) instead of K.
-constexpr int TC_CHUNK = 4;
-
 __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
   asm volatile(
       "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
@@ -139,55 +145,101 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
         "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
       : "r"(taddr));
 }
+// One warp writes 16 consecutive 32-bit columns of its 32 TMEM lanes.
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&v)[16]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};"
+      ::"r"(taddr), "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]),
+        "r"(v[8]), "r"(v[9]), "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15])
+      : "memory");
+}
 
-// Split one landed stage (both operands) into K-major hi/lo tiles.
-__device__ __forceinline__ void split_stage(uint8_t* st, int t, int a_kmajor, int b_kmajor) {
-#pragma unroll 1
-  for (int op = 0; op < 2; ++op) {
-    const bool kmaj = op == 0 ? a_kmajor : b_kmajor;
-    uint8_t* hi_t = st + op * TC_TILE_BYTES;
-    uint8_t* lo_t = st + (2 + op) * TC_TILE_BYTES;
-    if (kmaj) {
-      // landed K-major: split in place, lo into the twin buffer (same layout)
-      float4* hi = reinterpret_cast<float4*>(hi_t);
-      float4* lo = reinterpret_cast<float4*>(lo_t);
-#pragma unroll 4
-      for (int q = t; q < TC_TILE_BYTES / 16; q += 128) {
-        float4 x = hi[q], h, l;
-        const float* xv = &x.x;
-        float* hv = &h.x;
-        float* lv = &l.x;
+__device__ __forceinline__ float tf32_hi(float x) { return __uint_as_float(__float_as_uint(x) & 0xFFFFE000u); }
+
+// ------------------------------------------------------------------ kernel --
+// Accumulator chunking: the tensor core accumulates in f32 without
+// round-to-nearest on every add, so error grows with the number of
+// accumulation steps. The MMA warp therefore alternates between two TMEM
+// accumulators every TC_CHUNK K-stages (128 MMA-K), and the split/epilogue
+// warps drain each finished accumulator into per-thread f32 registers with
+// round-to-nearest adds; total error then grows like sqrt(K) instead of K.
+constexpr int TC_CHUNK = 4;
+
+// A tile row r (this thread's TMEM lane) -> hi/lo columns of the stage.
+// K-major landing: row r is 128 bytes, 16-byte chunk c stored at c ^ (r % 8).
+// MN-major landing: four 32(MN) x 32(K) boxes; element (k, m) of box m / 32
+// is in row k at chunk ((m % 32) / 4) ^ (k % 8): a warp reading one k reads
+// one 128-byte row, so every access is conflict-free.
+__device__ __forceinline__ void split_a_row(const uint8_t* a, int r, bool kmajor, uint32_t tcol) {
 #pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          float hh = __uint_as_float(__float_as_uint(xv[e]) & 0xFFFFE000u);
-          hv[e] = hh;
-          lv[e] = xv[e] - hh;
-        }
-        hi[q] = h;
-        lo[q] = l;
+  for (int h = 0; h < 2; ++h) {
+    float v[16];
+    if (kmajor) {
+      const uint8_t* row = a + r * 128;
+#pragma unroll
+      for (int c4 = 0; c4 < 4; ++c4) {
+        const int c = 4 * h + c4;
+        const float4 x = *reinterpret_cast<const float4*>(row + ((c ^ (r & 7)) << 4));
+        v[4 * c4] = x.x; v[4 * c4 + 1] = x.y; v[4 * c4 + 2] = x.z; v[4 * c4 + 3] = x.w;
       }
     } else {
-      // landed MN-major in staging: 4 boxes (MN chunk j) of 32 K-rows x
-      // 128 bytes; element (k, mn) sits in row k, 16-byte chunk
-      // (mn%32)/4 XOR (k%8). Write hi/lo transposed into the K-major
-      // tiles: element (mn, k) in row mn, chunk (k/4) XOR (mn%8).
-      const uint8_t* stg = st + (4 + op) * TC_TILE_BYTES;
-#pragma unroll 2
-      for (int q = t; q < TC_TILE_BYTES / 16; q += 128) {
-        const int j = q >> 8;
-        const int k = (q >> 3) & 31;
-        const int pc = q & 7;
-        const int lc = pc ^ (k & 7);
-        const float4 x = *reinterpret_cast<const float4*>(stg + q * 16);
-        const float* xv = &x.x;
+      const uint8_t* box = a + (r >> 5) * 4096;
+      const int m = r & 31;
 #pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const int mn = j * 32 + lc * 4 + e;
-          const uint32_t o = (uint32_t)mn * 128u + (uint32_t)((((k >> 2) ^ (mn & 7)) << 4) + ((k & 3) << 2));
-          const float hh = __uint_as_float(__float_as_uint(xv[e]) & 0xFFFFE000u);
-          *reinterpret_cast<float*>(hi_t + o) = hh;
-          *reinterpret_cast<float*>(lo_t + o) = xv[e] - hh;
-        }
+      for (int kk = 0; kk < 16; ++kk) {
+        const int k = 16 * h + kk;
+        v[kk] = *reinterpret_cast<const float*>(box + k * 128 + ((((m >> 2) ^ (k & 7))) << 4) + ((m & 3) << 2));
+      }
+    }
+    uint32_t hi[16], lo[16];
+#pragma unroll
+    for (int e = 0; e < 16; ++e) {
+      const float hh = tf32_hi(v[e]);
+      hi[e] = __float_as_uint(hh);
+      lo[e] = __float_as_uint(v[e] - hh);
+    }
+    tmem_st16(tcol + 16 * h, hi);
+    tmem_st16(tcol + 32 + 16 * h, lo);
+  }
+}
+
+// B tile -> K-major hi (slot 1) and lo (slot 2) tiles, 128 threads.
+__device__ __forceinline__ void split_b(uint8_t* st, int t, bool kmajor) {
+  uint8_t* hi_t = st + TC_TILE_BYTES;
+  uint8_t* lo_t = st + 2 * TC_TILE_BYTES;
+  if (kmajor) {
+    // landed K-major in slot 1: split in place, lo into slot 2 (same layout)
+    float4* hi = reinterpret_cast<float4*>(hi_t);
+    float4* lo = reinterpret_cast<float4*>(lo_t);
+#pragma unroll 4
+    for (int q = t; q < TC_TILE_BYTES / 16; q += 128) {
+      const float4 x = hi[q];
+      float4 h, l;
+      h.x = tf32_hi(x.x); h.y = tf32_hi(x.y); h.z = tf32_hi(x.z); h.w = tf32_hi(x.w);
+      l.x = x.x - h.x; l.y = x.y - h.y; l.z = x.z - h.z; l.w = x.w - h.w;
+      hi[q] = h;
+      lo[q] = l;
+    }
+  } else {
+    // landed MN-major in slot 3: 4 boxes (N chunk j) of 32 K-rows x 128
+    // bytes; element (k, n) sits in row k, 16-byte chunk (n%32)/4 XOR (k%8).
+    // Write hi/lo transposed: element (n, k) in row n, chunk (k/4) XOR (n%8).
+    const uint8_t* stg = st + 3 * TC_TILE_BYTES;
+#pragma unroll 2
+    for (int q = t; q < TC_TILE_BYTES / 16; q += 128) {
+      const int j = q >> 8;
+      const int k = (q >> 3) & 31;
+      const int pc = q & 7;
+      const int lc = pc ^ (k & 7);
+      const float4 x = *reinterpret_cast<const float4*>(stg + q * 16);
+      const float* xv = &x.x;
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int n = j * 32 + lc * 4 + e;
+        const uint32_t o = (uint32_t)n * 128u + (uint32_t)((((k >> 2) ^ (n & 7)) << 4) + ((k & 3) << 2));
+        const float hh = tf32_hi(xv[e]);
+        *reinterpret_cast<float*>(hi_t + o) = hh;
+        *reinterpret_cast<float*>(lo_t + o) = xv[e] - hh;
       }
     }
   }
@@ -253,10 +305,10 @@ __global__ void __launch_bounds__(192, 1) gemm_tc_kernel(const __grid_constant__
         const int k0 = (kbeg + it) * TC_BK;
         if (P.a_kmajor) tma_load_4d(&tmA, &full[s], st, k0, (int)m0, ab1, ab2);
         else for (int j = 0; j < 4; ++j)
-          tma_load_4d(&tmA, &full[s], st + 4 * TC_TILE_BYTES + j * 4096, (int)m0 + 32 * j, k0, ab1, ab2);
+          tma_load_4d(&tmA, &full[s], st + j * 4096, (int)m0 + 32 * j, k0, ab1, ab2);
         if (P.b_kmajor) tma_load_4d(&tmB, &full[s], st + TC_TILE_BYTES, k0, (int)n0, bb1, bb2);
         else for (int j = 0; j < 4; ++j)
-          tma_load_4d(&tmB, &full[s], st + 5 * TC_TILE_BYTES + j * 4096, (int)n0 + 32 * j, k0, bb1, bb2);
+          tma_load_4d(&tmB, &full[s], st + 3 * TC_TILE_BYTES + j * 4096, (int)n0 + 32 * j, k0, bb1, bb2);
         if (first_cta) g_gemm_tc_dbg[0] = it + 1;
       }
     }
@@ -277,22 +329,20 @@ __global__ void __launch_bounds__(192, 1) gemm_tc_kernel(const __grid_constant__
         if (!mbar_wait(&conv[s], ph, 2)) { ok = false; break; }
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
         const uint32_t base = smem_u32(smem + s * TC_STAGE_BYTES);
-        const uint32_t a_hi = base, b_hi = base + TC_TILE_BYTES;
-        const uint32_t a_lo = base + 2 * TC_TILE_BYTES, b_lo = base + 3 * TC_TILE_BYTES;
+        const uint32_t b_hi = base + TC_TILE_BYTES, b_lo = base + 2 * TC_TILE_BYTES;
+        const uint32_t a_hi = tmem + TC_ACOL + 64u * (uint32_t)s, a_lo = a_hi + 32u;
         const uint32_t dacc = tmem + (uint32_t)(acc * TC_BN);
 #pragma unroll
         for (int kk = 0; kk < TC_BK / 8; ++kk) {
-          // K-major tiles: 128 rows of 128 bytes (32 K values), 8-row groups
-          // 1 KB apart (SBO); a K step of 8 advances 32 bytes in the row.
-          const uint32_t off = kk * 32;
-          uint64_t dAh = umma_desc(a_hi + off, 16, 1024), dAl = umma_desc(a_lo + off, 16, 1024);
-          uint64_t dBh = umma_desc(b_hi + off, 16, 1024), dBl = umma_desc(b_lo + off, 16, 1024);
+          // B: 128 rows of 128 bytes (32 K values), 8-row groups 1 KB apart
+          // (SBO); a K step of 8 advances 32 bytes in the row. A: 8 columns.
+          const uint64_t dBh = umma_desc(b_hi + kk * 32, 16, 1024), dBl = umma_desc(b_lo + kk * 32, 16, 1024);
           const uint32_t first = (chunk_start && kk == 0) ? 0u : 1u;
-          umma_tf32(dacc, dAl, dBh, idesc, first);
-          umma_tf32(dacc, dAh, dBl, idesc, 1u);
-          umma_tf32(dacc, dAh, dBh, idesc, 1u);
+          umma_tf32_ts(dacc, a_lo + kk * 8, dBh, idesc, first);
+          umma_tf32_ts(dacc, a_hi + kk * 8, dBl, idesc, 1u);
+          umma_tf32_ts(dacc, a_hi + kk * 8, dBh, idesc, 1u);
         }
-        umma_commit(&empty[s]);  // frees the stage once these MMAs have read it
+        umma_commit(&empty[s]);  // frees the stage (smem and TMEM A) once these MMAs have read it
         if ((it % TC_CHUNK) == TC_CHUNK - 1 || it == nk - 1) umma_commit(&dfull[acc]);
         if (first_cta) g_gemm_tc_dbg[2] = it + 1;
       }
@@ -301,6 +351,8 @@ __global__ void __launch_bounds__(192, 1) gemm_tc_kernel(const __grid_constant__
     // ---------------------------------------- split, drain, then epilogue --
     const int t = threadIdx.x - 64;  // 0..127
     const int g = warp & 3;          // TMEM lane group this warp may access
+    const int r = g * 32 + lane;     // tile row = TMEM lane
+    const uint32_t lane_base = (uint32_t)(g * 32) << 16;
     float sum[TC_BN];
 #pragma unroll
     for (int j = 0; j < TC_BN; ++j) sum[j] = 0.f;
@@ -311,11 +363,11 @@ __global__ void __launch_bounds__(192, 1) gemm_tc_kernel(const __grid_constant__
       asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
 #pragma unroll
       for (int q = 0; q < TC_BN / 32; ++q) {
-        uint32_t r[32];
-        tmem_ld32(tmem + ((uint32_t)(g * 32) << 16) + (uint32_t)(acc * TC_BN + q * 32), r);
+        uint32_t v[32];
+        tmem_ld32(tmem + lane_base + (uint32_t)(acc * TC_BN + q * 32), v);
         asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 #pragma unroll
-        for (int j = 0; j < 32; ++j) sum[q * 32 + j] += __uint_as_float(r[j]);
+        for (int j = 0; j < 32; ++j) sum[q * 32 + j] += __uint_as_float(v[j]);
       }
       asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
       mbar_arrive(&dempty[acc]);
@@ -326,8 +378,11 @@ __global__ void __launch_bounds__(192, 1) gemm_tc_kernel(const __grid_constant__
       const uint32_t ph = (uint32_t)(it / TC_STAGES) & 1u;
       if (!mbar_wait(&full[s], ph, 3)) { ok = false; break; }
       uint8_t* st = smem + s * TC_STAGE_BYTES;
-      split_stage(st, t, P.a_kmajor, P.b_kmajor);
+      split_a_row(st, r, P.a_kmajor != 0, tmem + lane_base + TC_ACOL + 64u * (uint32_t)s);
+      split_b(st, t, P.b_kmajor != 0);
+      asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
       asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
       mbar_arrive(&conv[s]);
       if (t == 0 && first_cta) g_gemm_tc_dbg[1] = it + 1;
       // after splitting the last stage of chunk c+1, drain chunk c
@@ -342,47 +397,55 @@ __global__ void __launch_bounds__(192, 1) gemm_tc_kernel(const __grid_constant__
     }
     if (ok) {
       if (t == 0 && first_cta) g_gemm_tc_dbg[3] = 1;
-      const int64_t row = m0 + g * 32 + lane;
+      const int64_t row = m0 + r;
       // split-K: raw partial tile into the workspace, finished by gemm_splitk_reduce
       float* C = partial ? P.ws + ((int64_t)sp * P.batch + zb) * P.M * P.N
                          : P.C + (int64_t)i1 * P.c_batch + (int64_t)i2 * P.c_batch2;
-      const int64_t ldc = partial ? P.N : P.ldc;
+      const int64_t cm = partial ? P.N : P.c_m, cn = partial ? 1 : P.c_n;
       const float alpha = partial ? 1.f : P.alpha;
       const float* bias = partial ? nullptr : P.bias;
+      const bool bias_m = P.bias_m != 0;
       const int accumulate = partial ? 0 : P.accumulate;
       if (row < P.M) {
+        const float brow = (bias && bias_m) ? bias[row] : 0.f;
+        const float* bcol = (bias && !bias_m) ? bias : nullptr;
 #pragma unroll
         for (int q = 0; q < TC_BN / 32; ++q) {
           const int64_t col0 = n0 + q * 32;
           if (col0 >= P.N) break;
-          float* dst = C + row * ldc + col0;
-          const bool vec = (col0 + 32 <= P.N) && ((ldc & 3) == 0) &&
-                           ((reinterpret_cast<uintptr_t>(dst) & 15) == 0);
-          if (vec) {
+          if (cn == 1) {
+            float* dst = C + row * cm + col0;
+            const bool vec = (col0 + 32 <= P.N) && ((cm & 3) == 0) && ((reinterpret_cast<uintptr_t>(dst) & 15) == 0);
+            if (vec) {
 #pragma unroll
-            for (int j = 0; j < 32; j += 4) {
-              float4 v = make_float4(sum[q * 32 + j] * alpha, sum[q * 32 + j + 1] * alpha,
-                                     sum[q * 32 + j + 2] * alpha, sum[q * 32 + j + 3] * alpha);
-              if (bias) {
-                v.x += bias[col0 + j]; v.y += bias[col0 + j + 1];
-                v.z += bias[col0 + j + 2]; v.w += bias[col0 + j + 3];
+              for (int j = 0; j < 32; j += 4) {
+                float4 v = make_float4(sum[q * 32 + j] * alpha + brow, sum[q * 32 + j + 1] * alpha + brow,
+                                       sum[q * 32 + j + 2] * alpha + brow, sum[q * 32 + j + 3] * alpha + brow);
+                if (bcol) {
+                  v.x += bcol[col0 + j]; v.y += bcol[col0 + j + 1];
+                  v.z += bcol[col0 + j + 2]; v.w += bcol[col0 + j + 3];
+                }
+                float4* d4 = reinterpret_cast<float4*>(dst + j);
+                if (accumulate) {
+                  const float4 o = *d4;
+                  v.x += o.x; v.y += o.y; v.z += o.z; v.w += o.w;
+                }
+                *d4 = v;
               }
-              float4* d4 = reinterpret_cast<float4*>(dst + j);
-              if (accumulate) {
-                float4 o = *d4;
-                v.x += o.x; v.y += o.y; v.z += o.z; v.w += o.w;
-              }
-              *d4 = v;
+              continue;
             }
-          } else {
+          }
+          // general strides; with c_m == 1 (swapped operands) the 32 lanes
+          // write 32 consecutive floats per column
 #pragma unroll
-            for (int j = 0; j < 32; ++j) {
-              if (col0 + j < P.N) {
-                float v = sum[q * 32 + j] * alpha;
-                if (bias) v += bias[col0 + j];
-                if (accumulate) v += dst[j];
-                dst[j] = v;
-              }
+          for (int j = 0; j < 32; ++j) {
+            const int64_t col = col0 + j;
+            if (col < P.N) {
+              float v = sum[q * 32 + j] * alpha + brow;
+              if (bcol) v += bcol[col];
+              float* d = C + row * cm + col * cn;
+              if (accumulate) v += *d;
+              *d = v;
             }
           }
         }
@@ -397,19 +460,23 @@ __global__ void __launch_bounds__(192, 1) gemm_tc_kernel(const __grid_constant__
 }
 
 // Deterministic split-K reduction: C = alpha * sum_sp ws[sp] (+bias) (+C),
-// summed in split order.
+// summed in split order. Threads walk C's memory order (row-fastest after an
+// operand swap) so the stores coalesce; the partial tiles are L2-resident.
 __global__ void __launch_bounds__(256) gemm_splitk_reduce(const __grid_constant__ TcParams P) {
   const int64_t per = P.M * P.N;
   const int64_t total = per * P.batch;
   const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  const bool rowfast = P.c_m == 1 && P.c_n != 1;
   for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < total; e += stride) {
-    const int64_t zb = e / per, rem = e % per, row = rem / P.N, col = rem % P.N;
+    const int64_t zb = e / per, rem = e % per;
+    const int64_t row = rowfast ? rem % P.M : rem / P.N, col = rowfast ? rem / P.M : rem % P.N;
+    const int64_t w = zb * per + row * P.N + col;
     float v = 0.f;
-    for (int sp = 0; sp < P.splits; ++sp) v += P.ws[(int64_t)sp * total + e];
+    for (int sp = 0; sp < P.splits; ++sp) v += P.ws[(int64_t)sp * total + w];
     v *= P.alpha;
-    if (P.bias) v += P.bias[col];
+    if (P.bias) v += P.bias[P.bias_m ? row : col];
     const int64_t i1 = zb / P.batch2, i2 = zb % P.batch2;
-    float* d = P.C + i1 * P.c_batch + i2 * P.c_batch2 + row * P.ldc + col;
+    float* d = P.C + i1 * P.c_batch + i2 * P.c_batch2 + row * P.c_m + col * P.c_n;
     *d = P.accumulate ? *d + v : v;
   }
 }
@@ -429,7 +496,8 @@ static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
   return fn;
 }
 
-// Tensor map for one operand. kmajor: dims {K, MN, b1, b2}; else {MN, K, b1, b2}.
+// Tensor map for one operand. kmajor: dims {K, MN, b1, b2}, box {32, 128};
+// else {MN, K, b1, b2}, box {32, 32} (four boxes cover a 128-wide tile).
 static bool make_map(CUtensorMap* tm, const float* base, bool kmajor, int64_t mn, int64_t k, int64_t ld_mn,
                      int64_t ld_k, int64_t e1, int64_t s1, int64_t e2, int64_t s2) {
   auto fn = encode_fn();
@@ -489,33 +557,40 @@ bool launch_gemm_tc(const GemmDesc& g, cudaStream_t s) {
   if (!tc_enabled()) return false;
   // Tiny contractions are cheaper on CUDA cores than a 128x128 tile pipeline.
   if (g.M * g.N * g.K < (int64_t)64 * 64 * 64 || g.K < 16) return false;
-  const bool a_k = g.lda_k == 1, a_mn = g.lda_m == 1;
-  const bool b_k = g.ldb_k == 1, b_mn = g.ldb_n == 1;
-  if (!(a_k || a_mn) || !(b_k || b_mn)) return false;
   if ((reinterpret_cast<uintptr_t>(g.A) & 15) || (reinterpret_cast<uintptr_t>(g.B) & 15)) return false;
   if (g.M > INT32_MAX || g.N > INT32_MAX || g.K > INT32_MAX) return false;
+  // Operand roles. B must be K-major in shared memory; when only A is,
+  // compute C^T = B^T A^T instead (A' = B^T, B' = A^T, C' = C^T).
+  const bool swap = g.ldb_k != 1 && g.lda_k == 1;
+  int64_t M = g.M, N = g.N;
+  const float *A = g.A, *B = g.B;
+  int64_t a_m = g.lda_m, a_k = g.lda_k, a_b = g.a_batch, a_b2 = g.a_batch2;
+  int64_t b_n = g.ldb_n, b_k = g.ldb_k, b_b = g.b_batch, b_b2 = g.b_batch2;
+  int64_t c_m = g.ldc, c_n = 1;
+  if (swap) {
+    std::swap(M, N);
+    A = g.B; a_m = g.ldb_n; a_k = g.ldb_k; a_b = g.b_batch; a_b2 = g.b_batch2;
+    B = g.A; b_n = g.lda_m; b_k = g.lda_k; b_b = g.a_batch; b_b2 = g.a_batch2;
+    c_m = 1; c_n = g.ldc;
+  }
+  const bool ak = a_k == 1, bk = b_k == 1;
+  if (!(ak || a_m == 1) || !(bk || b_n == 1)) return false;
   const int64_t b2 = g.batch2 > 0 ? g.batch2 : 1;
   const int64_t b1 = g.batch / b2;
   CUtensorMap ta, tb;
-  const bool ak = a_k;  // prefer K-major when both hold (degenerate dims)
-  const bool bk = b_k;
-  if (!make_map(&ta, g.A, ak, g.M, g.K, g.lda_m, g.lda_k, g.a_batch ? b1 : 1, g.a_batch, g.a_batch2 ? b2 : 1,
-                g.a_batch2))
-    return false;
-  if (!make_map(&tb, g.B, bk, g.N, g.K, g.ldb_n, g.ldb_k, g.b_batch ? b1 : 1, g.b_batch, g.b_batch2 ? b2 : 1,
-                g.b_batch2))
-    return false;
+  if (!make_map(&ta, A, ak, M, g.K, a_m, a_k, a_b ? b1 : 1, a_b, a_b2 ? b2 : 1, a_b2)) return false;
+  if (!make_map(&tb, B, bk, N, g.K, b_n, b_k, b_b ? b1 : 1, b_b, b_b2 ? b2 : 1, b_b2)) return false;
   TcParams p{};
-  p.M = g.M; p.N = g.N; p.K = g.K;
+  p.M = M; p.N = N; p.K = g.K;
   p.batch = g.batch; p.batch2 = b2;
   p.a_kmajor = ak ? 1 : 0; p.b_kmajor = bk ? 1 : 0;
-  p.a_b1 = g.a_batch ? 1 : 0; p.a_b2 = g.a_batch2 ? 1 : 0;
-  p.b_b1 = g.b_batch ? 1 : 0; p.b_b2 = g.b_batch2 ? 1 : 0;
-  p.C = g.C; p.ldc = g.ldc; p.c_batch = g.c_batch; p.c_batch2 = g.c_batch2;
-  p.bias = g.bias; p.alpha = g.alpha; p.accumulate = g.accumulate;
+  p.a_b1 = a_b ? 1 : 0; p.a_b2 = a_b2 ? 1 : 0;
+  p.b_b1 = b_b ? 1 : 0; p.b_b2 = b_b2 ? 1 : 0;
+  p.C = g.C; p.c_m = c_m; p.c_n = c_n; p.c_batch = g.c_batch; p.c_batch2 = g.c_batch2;
+  p.bias = g.bias; p.bias_m = swap ? 1 : 0; p.alpha = g.alpha; p.accumulate = g.accumulate;
   const int64_t nk = (g.K + TC_BK - 1) / TC_BK;
-  int splits = gemm_tc_splits(g.M, g.N, g.K, g.batch);
-  if (splits > 1 && (!g.workspace || g.workspace_floats < (int64_t)splits * g.batch * g.M * g.N)) splits = 1;
+  int splits = gemm_tc_splits(M, N, g.K, g.batch);
+  if (splits > 1 && (!g.workspace || g.workspace_floats < (int64_t)splits * g.batch * M * N)) splits = 1;
   p.kps = (int)((nk + splits - 1) / splits);
   splits = (int)((nk + p.kps - 1) / p.kps);  // every split gets at least one K-stage
   p.splits = splits;
@@ -527,11 +602,10 @@ bool launch_gemm_tc(const GemmDesc& g, cudaStream_t s) {
       return false;
     attr = true;
   }
-  dim3 grid((unsigned)((g.N + TC_BN - 1) / TC_BN), (unsigned)((g.M + TC_BM - 1) / TC_BM),
-            (unsigned)(g.batch * splits));
+  dim3 grid((unsigned)((N + TC_BN - 1) / TC_BN), (unsigned)((M + TC_BM - 1) / TC_BM), (unsigned)(g.batch * splits));
   gemm_tc_kernel<<<grid, 192, TC_SMEM, s>>>(ta, tb, p);
   if (splits > 1) {
-    int64_t total = g.batch * g.M * g.N;
+    int64_t total = g.batch * M * N;
     int64_t blocks = (total + 255) / 256, cap = (int64_t)device_sm_count() * 8;
     gemm_splitk_reduce<<<(unsigned)(blocks < cap ? blocks : cap), 256, 0, s>>>(p);
   }
