@@ -126,12 +126,13 @@ struct GemmDesc {
   int64_t M, N, K, batch;  // batch index z = i1 * batch2 + i2, i1 < batch / batch2
   const float* A; int64_t lda_m, lda_k, a_batch;  // A(m,k) = A[m*lda_m + k*lda_k]
   const float* B; int64_t ldb_k, ldb_n, b_batch;  // B(k,n) = B[k*ldb_k + n*ldb_n]
-  float* C; int64_t ldc, c_batch;                 // C(m,n) = C[m*ldc + n]
+  float* C; int64_t ldc, c_batch;                 // C(m,n) = C[m*ldc + n*ldc_n]
   const float* bias;                              // optional [N], added in the epilogue
   float alpha;
   int accumulate;                                 // C += result
   int64_t batch2;                                 // inner batch extent (1 = single batch dim)
   int64_t a_batch2, b_batch2, c_batch2;           // strides of the inner batch index
+  int64_t ldc_n;                                  // C column stride (0 is read as 1)
   float* workspace;                               // split-K partial tiles (may be null)
   int64_t workspace_floats;
 };

@@ -65,7 +65,7 @@ __global__ void __launch_bounds__(256) sgemm_kernel(const __grid_constant__ Gemm
       if (gn >= g.N) continue;
       float v = acc[i][j] * g.alpha;
       if (g.bias) v += g.bias[gn];
-      float* c = C + gm * g.ldc + gn;
+      float* c = C + gm * g.ldc + gn * (g.ldc_n ? g.ldc_n : 1);
       *c = g.accumulate ? *c + v : v;
     }
   }

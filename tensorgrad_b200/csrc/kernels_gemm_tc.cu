@@ -566,12 +566,12 @@ bool launch_gemm_tc(const GemmDesc& g, cudaStream_t s) {
   const float *A = g.A, *B = g.B;
   int64_t a_m = g.lda_m, a_k = g.lda_k, a_b = g.a_batch, a_b2 = g.a_batch2;
   int64_t b_n = g.ldb_n, b_k = g.ldb_k, b_b = g.b_batch, b_b2 = g.b_batch2;
-  int64_t c_m = g.ldc, c_n = 1;
+  int64_t c_m = g.ldc, c_n = g.ldc_n ? g.ldc_n : 1;
   if (swap) {
     std::swap(M, N);
     A = g.B; a_m = g.ldb_n; a_k = g.ldb_k; a_b = g.b_batch; a_b2 = g.b_batch2;
     B = g.A; b_n = g.lda_m; b_k = g.lda_k; b_b = g.a_batch; b_b2 = g.a_batch2;
-    c_m = 1; c_n = g.ldc;
+    std::swap(c_m, c_n);
   }
   const bool ak = a_k == 1, bk = b_k == 1;
   if (!(ak || a_m == 1) || !(bk || b_n == 1)) return false;

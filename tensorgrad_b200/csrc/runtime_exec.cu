@@ -165,7 +165,14 @@ void Graph::plan_storage() {
     // A fused elementwise group runs at its root op: its members' operands are
     // read there, and values passed inside the group need no storage.
     const int pos = ew_pos(i);
-    if (views_[o].root == o && !ew_internal(o)) { used[o] = 1; if (def[o] < 0) def[o] = i; end[o] = std::max(end[o], i); }
+    // The op writes its output's root: its own storage, or (for a GEMM or
+    // permute writing straight into a later permute's layout) that root.
+    if (!views_[o].onehot && !ew_internal(o)) {
+      const int r = views_[o].root;
+      used[r] = 1;
+      if (def[r] < 0 || i < def[r]) def[r] = i;
+      end[r] = std::max(end[r], i);
+    }
     if (action_[i] == 100 || action_[i] == 101) {
       int a = P.op(i)["a"].i32();
       int oh = action_[i] == 100 ? a : P.op(P.producer[P.op(P.producer[a])["a"].i32()])["a"].i32();
@@ -683,23 +690,28 @@ void Graph::emit_launches() {
       g.C = reinterpret_cast<float*>(ptr(o));
       g.lda_m = va.strides[ra - 2]; g.lda_k = va.strides[ra - 1];
       g.ldb_k = vb.strides[rb - 2]; g.ldb_n = vb.strides[rb - 1];
-      g.ldc = g.N;
+      // C may be a strided view (written straight into a later permute's layout)
+      const TView& vc = views_[o];
+      const int rc = (int)os.size();
+      g.ldc = vc.strides[rc - 2];
+      g.ldc_n = vc.strides[rc - 1];
       g.batch2 = 1;
-      // batch dims (output contiguous [..., M, N])
       std::vector<int64_t> bd(os.begin(), os.end() - 2), sa, sb, sc;
       int nb = (int)bd.size();
-      auto ocs = cstrides(os);
       for (int d = 0; d < nb; ++d) {
         sa.push_back(va.strides[d]);
         sb.push_back(k == "matmul" ? 0 : vb.strides[d]);
-        sc.push_back(ocs[d]);
+        sc.push_back(vc.strides[d]);
       }
       g.M = as[ra - 2];
-      // matmul: fold leading dims into M when A's layout allows it
+      // matmul: fold leading dims into M when A's and C's layouts allow it
       if (k == "matmul") {
         bool fold = true;
-        int64_t expect = g.lda_m * g.M;
-        for (int d = nb - 1; d >= 0; --d) { if (sa[d] != expect && bd[d] != 1) fold = false; expect *= bd[d]; }
+        int64_t expect = g.lda_m * g.M, expect_c = g.ldc * g.M;
+        for (int d = nb - 1; d >= 0; --d) {
+          if (bd[d] != 1 && (sa[d] != expect || sc[d] != expect_c)) fold = false;
+          expect *= bd[d]; expect_c *= bd[d];
+        }
         if (fold) { int64_t m = g.M; for (auto x : bd) m *= x; g.M = m; bd.clear(); sa.clear(); sb.clear(); sc.clear(); nb = 0; }
       }
       // drop unit dims, merge adjacent batch dims that all three operands allow
@@ -744,7 +756,7 @@ void Graph::emit_launches() {
         if (!va.contiguous) throw TgError("Error", "internal: reshape of a strided view");
         in_str = cstrides(os);
       }
-      emit_copy(a, extra, os, in_str, ptr(o), cstrides(os), k);
+      emit_copy(a, extra, os, in_str, ptr(o), views_[o].strides, k);
       continue;
     }
     if (k == "concat") {

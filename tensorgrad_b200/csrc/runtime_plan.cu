@@ -169,6 +169,17 @@ void Graph::plan_views() {
     }
   }
 
+  // A permute is a view when everything that reads it takes strided operands:
+  // GEMMs, or permutes that are views themselves (decided back to front).
+  std::vector<char> pview(nO, 0);
+  for (int i = nO - 1; i >= 0; --i) {
+    if (op_done_[i] || P.kind[i] != "permute" || pinned.count(P.out[i])) continue;
+    bool ok = !P.consumers[P.out[i]].empty();
+    for (int c : P.consumers[P.out[i]])
+      if (!((is_gemm(c) && action_[c] < 100) || (P.kind[c] == "permute" && pview[c]))) ok = false;
+    pview[i] = ok;
+  }
+
   // Zero-copy views, in op order so chains resolve.
   for (int i = 0; i < nO; ++i) {
     if (op_done_[i]) continue;
@@ -201,9 +212,7 @@ void Graph::plan_views() {
       int a = P.op(i)["a"].i32();
       const TView& va = views_[a];
       if (va.onehot) continue;
-      bool all_gemm = !P.consumers[o].empty();
-      for (int c : P.consumers[o]) if (!is_gemm(c) || action_[c] >= 100) all_gemm = false;
-      if (!all_gemm) continue;
+      if (!pview[i]) continue;
       const auto& perm = P.op(i)["perm"].a;
       views_[o].root = va.root;
       views_[o].off = va.off;
@@ -212,6 +221,38 @@ void Graph::plan_views() {
       views_[o].contiguous = false;
       op_done_[i] = 1;
     }
+  }
+
+  // Producer-side views: a permute whose input is written by a GEMM (or by
+  // another permute) and read by nothing else is done by that writer, which
+  // stores straight into the permuted layout through its output strides
+  // (attention's mergeHeads, and the head-split gradients). Back to front,
+  // so a chain of permutes collapses into its first writer.
+  std::set<int> observable = pinned;
+  for (auto& g : P.grads) observable.insert(g.second);
+  if (P.loss >= 0) observable.insert(P.loss);
+  for (int i = nO - 1; i >= 0; --i) {
+    if (op_done_[i] || P.kind[i] != "permute") continue;
+    int a = P.op(i)["a"].i32(), o = P.out[i];
+    const TView& va = views_[a];
+    if (va.root != a || !va.contiguous || va.onehot || observable.count(a)) continue;
+    if (P.consumers[a].size() != 1 || P.consumers[a][0] != i) continue;
+    int p = P.producer[a];
+    if (p < 0 || op_done_[p] || action_[p] != 0) continue;
+    const bool gemm_writer = is_gemm(p) && P.T[a].shape.size() <= 4;
+    const bool perm_writer = P.kind[p] == "permute";
+    if (!gemm_writer && !perm_writer) continue;
+    const TView& vo = views_[o];
+    if (vo.onehot) continue;
+    const auto& perm = P.op(i)["perm"].a;
+    TView nv;
+    nv.root = vo.root;
+    nv.off = vo.off;
+    nv.strides.assign(perm.size(), 0);
+    for (size_t d = 0; d < perm.size(); ++d) nv.strides[perm[d].i32()] = vo.strides[d];
+    nv.contiguous = nv.strides == contig_strides(P.T[a].shape);
+    views_[a] = nv;
+    op_done_[i] = 1;
   }
 }
 
