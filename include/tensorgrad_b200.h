@@ -94,6 +94,14 @@ int tg_read_tensor(tg_ctx* ctx, int graph_id, int tensor_id, void* out);
 /* Newline-separated kind of every kernel launch in one step. */
 int tg_launch_list(tg_ctx* ctx, int graph_id, char* buf, size_t cap, size_t* needed);
 
+/* Plans a program without a GPU and writes JSON {"info", "launches",
+ * "kernelSources"}: the graph info, the label of every launch one step would
+ * make, and the CUDA source of every fused elementwise kernel. No device
+ * memory is allocated and nothing is compiled or run. No counterpart in the
+ * reference (its codegen.ts plan is only visible through the WGSL it emits);
+ * used to test planner decisions on machines without a GPU. */
+int tg_plan_dry(const char* program_json, size_t len, int world, char* buf, size_t cap, size_t* needed);
+
 /* Runs one step launch by launch with CUDA events around each launch and
  * writes per-launch milliseconds (in tg_launch_list order). */
 int tg_profile_step(tg_ctx* ctx, int graph_id, float* ms_out, int cap, int* n_out);

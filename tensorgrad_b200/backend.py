@@ -21,7 +21,7 @@ EXPORTED = [
     "tg_nccl_unique_id", "tg_ctx_create", "tg_ctx_destroy", "tg_graph_create", "tg_graph_info",
     "tg_upload_params", "tg_download_params", "tg_step", "tg_run", "tg_set_inputs", "tg_launch_step",
     "tg_read_loss", "tg_stream", "tg_reset_optimizer", "tg_set_lr", "tg_destroy_graph", "tg_read_grad",
-    "tg_read_tensor", "tg_launch_list", "tg_profile_step", "tg_debug_gemm_error", "tg_debug_gemm_dbg", "tg_colsum_noalloc", "tg_last_error_name", "tg_last_error_message",
+    "tg_read_tensor", "tg_launch_list", "tg_profile_step", "tg_debug_gemm_error", "tg_debug_gemm_dbg", "tg_colsum_noalloc", "tg_plan_dry", "tg_last_error_name", "tg_last_error_message",
 ]
 
 
@@ -78,6 +78,7 @@ def load(path: str = LIB_PATH):
         "tg_debug_gemm_error": [ip],
         "tg_debug_gemm_dbg": [C.POINTER(C.c_int)],
         "tg_colsum_noalloc": [vp, vp, C.c_int64, C.c_int64, vp],
+        "tg_plan_dry": [C.c_char_p, sz, ip, C.c_char_p, sz, szp],
     }
     for name, args in sig.items():
         f = getattr(lib, name)
@@ -102,6 +103,20 @@ def _check(rc: int) -> None:
 def _names(names: Sequence[str]):
     arr = (C.c_char_p * len(names))(*[n.encode() for n in names])
     return arr
+
+
+def plan_dry(program: dict, world: int = 1) -> dict:
+    """Plans `program` without a GPU (views, fusion, storage, launches).
+
+    Returns {"info": ..., "launches": [label per kernel launch of one step],
+    "kernelSources": [CUDA source of each fused elementwise kernel]}."""
+    lib = load()
+    data = json.dumps(program, separators=(",", ":")).encode()
+    need = C.c_size_t()
+    _check(lib.tg_plan_dry(data, len(data), world, None, 0, C.byref(need)))
+    buf = C.create_string_buffer(need.value + 1)
+    _check(lib.tg_plan_dry(data, len(data), world, buf, len(buf), C.byref(need)))
+    return json.loads(buf.value.decode())
 
 
 def nccl_unique_id() -> bytes:

@@ -53,7 +53,7 @@ def build(verbose: bool = False) -> str:
     objs = [o for o, _ in results]
     changed = any(c for _, c in results)
     if changed or not os.path.exists(LIB) or os.path.getmtime(LIB) < max(os.path.getmtime(o) for o in objs):
-        cmd = [NVCC, *ARCH, "-shared", "-o", LIB, *objs, "-cudart", "static", *_nccl_link(), "-lcuda",
+        cmd = [NVCC, *ARCH, "-shared", "-o", LIB, *objs, "-cudart", "static", *_nccl_link(),
                "-L/usr/local/cuda/lib64", "-lnvrtc", "-Xlinker", "-rpath=/usr/local/cuda/lib64"]
         r = subprocess.run(cmd, capture_output=True, text=True)
         if r.returncode != 0:

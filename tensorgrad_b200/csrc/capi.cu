@@ -115,6 +115,36 @@ int tg_graph_info(tg_ctx* ctx, int graph_id, char* buf, size_t cap, size_t* need
   return guarded([&] { write_str(get_graph(ctx, graph_id)->info_json(), buf, cap, needed); });
 }
 
+int tg_plan_dry(const char* program_json, size_t len, int world, char* buf, size_t cap, size_t* needed) {
+  return guarded([&] {
+    if (world < 1) throw tg::TgError("Error", "tg_plan_dry: world must be >= 1");
+    tg::Context c(tg::Context::Dry{}, world);
+    tg::Graph g(&c, 0, nullptr, program_json, len);
+    std::string s = "{\"info\":" + g.info_json() + ",\"launches\":[";
+    auto q = [](const std::string& x) {
+      std::string o = "\"";
+      for (char ch : x) {
+        if (ch == '"' || ch == '\\') { o += '\\'; o += ch; }
+        else if (ch == '\n') o += "\\n";
+        else o += ch;
+      }
+      return o + "\"";
+    };
+    std::string kinds = g.launch_kinds();
+    size_t st = 0;
+    bool first = true;
+    for (size_t e; (e = kinds.find('\n', st)) != std::string::npos; st = e + 1) {
+      if (!first) s += ",";
+      first = false;
+      s += q(kinds.substr(st, e - st));
+    }
+    s += "],\"kernelSources\":[";
+    for (size_t i = 0; i < g.jit_sources().size(); ++i) s += (i ? "," : "") + q(g.jit_sources()[i]);
+    s += "]}";
+    write_str(s, buf, cap, needed);
+  });
+}
+
 int tg_launch_list(tg_ctx* ctx, int graph_id, char* buf, size_t cap, size_t* needed) {
   return guarded([&] { write_str(get_graph(ctx, graph_id)->launch_kinds(), buf, cap, needed); });
 }

@@ -8,6 +8,7 @@
 // identical groups (the same layer pattern repeated, or a second graph of the
 // same model) compile once.
 #include <cuda.h>
+#include <cudaTypedefs.h>
 #include <nvrtc.h>
 
 #include <cstdio>
@@ -38,6 +39,39 @@ std::string nvrtc_err(nvrtcProgram prog, nvrtcResult r, const char* what) {
     }
   }
   return msg;
+}
+// Driver entry points, resolved through the runtime so that the library
+// itself does not depend on libcuda (it loads on machines without a driver,
+// where only planning runs).
+struct DriverFns {
+  PFN_cuModuleLoadData_v2000 load = nullptr;
+  PFN_cuModuleGetFunction_v2000 get = nullptr;
+  PFN_cuLaunchKernel_v4000 launch = nullptr;
+  PFN_cuGetErrorString_v6000 err = nullptr;
+};
+const DriverFns& drv() {
+  static DriverFns d;
+  static bool done = false;
+  if (!done) {
+    auto sym = [](const char* name) -> void* {
+      void* p = nullptr;
+      cudaDriverEntryPointQueryResult q;
+      if (cudaGetDriverEntryPoint(name, &p, cudaEnableDefault, &q) != cudaSuccess || q != cudaDriverEntryPointSuccess)
+        throw TgError("CudaError", std::string("driver entry point ") + name + " unavailable");
+      return p;
+    };
+    d.load = reinterpret_cast<PFN_cuModuleLoadData_v2000>(sym("cuModuleLoadData"));
+    d.get = reinterpret_cast<PFN_cuModuleGetFunction_v2000>(sym("cuModuleGetFunction"));
+    d.launch = reinterpret_cast<PFN_cuLaunchKernel_v4000>(sym("cuLaunchKernel"));
+    d.err = reinterpret_cast<PFN_cuGetErrorString_v6000>(sym("cuGetErrorString"));
+    done = true;
+  }
+  return d;
+}
+std::string cu_err(CUresult r) {
+  const char* s = nullptr;
+  if (drv().err) drv().err(r, &s);
+  return s ? s : "CUresult " + std::to_string((int)r);
 }
 }  // namespace
 
@@ -88,16 +122,12 @@ void jit_compile_pending() {
     nvrtcDestroyProgram(&prog);
     if (r != NVRTC_SUCCESS) throw TgError("CompileError", nvrtc_err(nullptr, r, "cubin"));
     CUmodule mod = nullptr;
-    CUresult cr = cuModuleLoadData(&mod, cubin.data());
-    if (cr != CUDA_SUCCESS) {
-      const char* s = nullptr;
-      cuGetErrorString(cr, &s);
-      throw TgError("CudaError", std::string("cuModuleLoadData: ") + (s ? s : "?"));
-    }
+    CUresult cr = drv().load(&mod, cubin.data());
+    if (cr != CUDA_SUCCESS) throw TgError("CudaError", "cuModuleLoadData: " + cu_err(cr));
     for (auto& kv : by_src) {
       CUfunction fn = nullptr;
-      cr = cuModuleGetFunction(&fn, mod, kv.second.c_str());
-      if (cr != CUDA_SUCCESS) throw TgError("CudaError", "cuModuleGetFunction " + kv.second);
+      cr = drv().get(&fn, mod, kv.second.c_str());
+      if (cr != CUDA_SUCCESS) throw TgError("CudaError", "cuModuleGetFunction " + kv.second + ": " + cu_err(cr));
       g_fn_cache[{dev, kv.first}] = fn;
     }
   }
@@ -107,13 +137,9 @@ void jit_compile_pending() {
 
 void jit_launch(const JitFn& f, unsigned grid, unsigned block, void** args, cudaStream_t s) {
   if (!f.fn) throw TgError("Error", "internal: kernel " + f.name + " was not compiled");
-  CUresult r = cuLaunchKernel(reinterpret_cast<CUfunction>(f.fn), grid, 1, 1, block, 1, 1, 0,
-                              reinterpret_cast<CUstream>(s), args, nullptr);
-  if (r != CUDA_SUCCESS) {
-    const char* m = nullptr;
-    cuGetErrorString(r, &m);
-    throw TgError("CudaError", std::string("launch ") + f.name + ": " + (m ? m : "?"));
-  }
+  CUresult r = drv().launch(reinterpret_cast<CUfunction>(f.fn), grid, 1, 1, block, 1, 1, 0,
+                            reinterpret_cast<CUstream>(s), args, nullptr);
+  if (r != CUDA_SUCCESS) throw TgError("CudaError", "launch " + f.name + ": " + cu_err(r));
 }
 
 // Device helpers every generated kernel may use. Arithmetic goes through the

@@ -145,6 +145,7 @@ class Graph {
   int64_t param_numel(const std::string& name) const;
   int launches_per_step() const { return (int)launches_.size(); }
   std::string launch_kinds() const;
+  const std::vector<std::string>& jit_sources() const { return jit_sources_; }
   // Runs one step launch by launch (no CUDA graph) with events around each
   // launch; fills per-launch milliseconds.
   void profile_step(std::vector<float>& ms);
@@ -174,6 +175,7 @@ class Graph {
   std::vector<int> op_done_;         // ops folded away
   std::vector<int> ew_root_;         // per op: root op of its fused elementwise group, or -1
   bool jit_ = false;                 // fused elementwise groups compiled at plan time
+  std::vector<std::string> jit_sources_;  // generated kernel sources (planning-only contexts)
   void* arena_[AR_COUNT] = {};
   int64_t arena_bytes_[AR_COUNT] = {};
   bool arena_owned_[AR_COUNT] = {};
@@ -211,8 +213,14 @@ class Graph {
 class Context {
  public:
   Context(int device, int rank, int world, const unsigned char* nccl_id);
+  // Planning-only context: no device, stream or communicator. Graphs created
+  // on it are planned in full (views, fusion, storage, launch list, generated
+  // kernel sources) against placeholder arena addresses and never run.
+  struct Dry {};
+  Context(Dry, int world);
   ~Context();
   int device, rank, world;
+  bool dry = false;
   cudaStream_t stream = nullptr;
   void* nccl = nullptr;  // ncclComm_t
   std::map<int, std::unique_ptr<Graph>> graphs;

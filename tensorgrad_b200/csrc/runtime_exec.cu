@@ -58,7 +58,7 @@ Graph::Graph(Context* c, int gid, Graph* par, const char* json, size_t len) : id
   P.parse(json, len);
   const char* ng = getenv("TG_NO_GRAPH");
   use_graph_ = !(ng && ng[0] == '1');
-  TG_CUDA(cudaMallocHost(&loss_host_, 64));
+  if (!ctx->dry) TG_CUDA(cudaMallocHost(&loss_host_, 64));
   plan();
 }
 
@@ -83,7 +83,7 @@ void Graph::plan() {
                            "does not match the Adam/AdamW/SGD update patterns");
   plan_fusion();
   plan_storage();
-  init_constants();
+  if (!ctx->dry) init_constants();
   emit_launches();
 }
 
@@ -293,6 +293,11 @@ void Graph::plan_storage() {
   for (int a = 0; a < AR_COUNT; ++a) {
     arena_bytes_[a] = bump[a];
     if (bump[a] > 0) {
+      if (ctx->dry) {
+        // placeholder, 1 TiB apart per arena: only addresses are computed
+        arena_[a] = reinterpret_cast<void*>((uintptr_t)(a + 1) << 40);
+        continue;
+      }
       TG_CUDA(cudaMalloc(&arena_[a], (size_t)bump[a]));
       arena_owned_[a] = true;
       TG_CUDA(cudaMemset(arena_[a], 0, (size_t)bump[a]));
@@ -310,6 +315,7 @@ void Graph::plan_storage() {
       place(p.second, AR_PARAM, it->second);
     }
   }
+  if (ctx->dry) return;
   // State init values
   for (auto& s : P.states) {
     int t = s.tensor;
@@ -902,7 +908,7 @@ void Graph::emit_launches() {
       launch_scale(la, 1, inv, s);
     });
   }
-  jit_compile_pending();
+  if (!ctx->dry) jit_compile_pending();
 }
 
 // ------------------------------------------------------------ execution --
@@ -1135,6 +1141,8 @@ Context::Context(int dev, int rk, int wd, const unsigned char* nccl_id) : device
     nccl = comm;
   }
 }
+
+Context::Context(Dry, int wd) : device(-1), rank(0), world(wd), dry(true) {}
 
 Context::~Context() {
   graphs.clear();

@@ -304,7 +304,14 @@ void Graph::emit_ew_group(int r, const int* seed_ptr,
   char name[40];
   snprintf(name, sizeof name, "tgew_%016zx", std::hash<std::string>{}(body));
   std::string src = std::string("extern \"C\" __global__ void __launch_bounds__(256) ") + name + body;
-  auto fn = jit_request(name, src);
+  std::shared_ptr<JitFn> fn;
+  if (ctx->dry) {
+    jit_sources_.push_back(src);
+    fn = std::make_shared<JitFn>();
+    fn->name = name;
+  } else {
+    fn = jit_request(name, src);
+  }
 
   struct Args {
     std::vector<const void*> in;
