@@ -111,6 +111,12 @@ int tg_profile_step(tg_ctx* ctx, int graph_id, float* ms_out, int cap, int* n_ou
 int tg_debug_gemm_error(int reset);
 /* Progress markers of the first GEMM tile (8 ints) for pipeline diagnosis. */
 int tg_debug_gemm_dbg(int* out8);
+/* Pipeline timeline (SM clock cycles) of the first CTA of the last tcgen05
+ * GEMM launched with TG_GEMM_TRACE=1 in the environment: 6 rows of 64
+ * (TMA issued, stage landed, split done, MMAs issued per K-stage; chunk
+ * drained; start / epilogue start / epilogue end). Returns the number of
+ * values written (384) or -1. Debugging aid with no reference counterpart. */
+int tg_debug_gemm_trace(long long* out, int cap);
 
 /* Column sums of a row-major [outer, inner] f32 matrix already on the device
  * (out[j] = sum_i x[i*inner + j]), enqueued on `stream` (a cudaStream_t; NULL

@@ -21,7 +21,7 @@ EXPORTED = [
     "tg_nccl_unique_id", "tg_ctx_create", "tg_ctx_destroy", "tg_graph_create", "tg_graph_info",
     "tg_upload_params", "tg_download_params", "tg_step", "tg_run", "tg_set_inputs", "tg_launch_step",
     "tg_read_loss", "tg_stream", "tg_reset_optimizer", "tg_set_lr", "tg_destroy_graph", "tg_read_grad",
-    "tg_read_tensor", "tg_launch_list", "tg_profile_step", "tg_debug_gemm_error", "tg_debug_gemm_dbg", "tg_colsum_noalloc", "tg_plan_dry", "tg_last_error_name", "tg_last_error_message",
+    "tg_read_tensor", "tg_launch_list", "tg_profile_step", "tg_debug_gemm_error", "tg_debug_gemm_dbg", "tg_debug_gemm_trace", "tg_colsum_noalloc", "tg_plan_dry", "tg_last_error_name", "tg_last_error_message",
 ]
 
 
@@ -77,6 +77,7 @@ def load(path: str = LIB_PATH):
         "tg_profile_step": [vp, ip, C.POINTER(C.c_float), ip, C.POINTER(C.c_int)],
         "tg_debug_gemm_error": [ip],
         "tg_debug_gemm_dbg": [C.POINTER(C.c_int)],
+        "tg_debug_gemm_trace": [C.POINTER(C.c_longlong), ip],
         "tg_colsum_noalloc": [vp, vp, C.c_int64, C.c_int64, vp],
         "tg_plan_dry": [C.c_char_p, sz, ip, C.c_char_p, sz, szp],
     }

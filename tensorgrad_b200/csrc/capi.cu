@@ -241,6 +241,7 @@ int tg_profile_step(tg_ctx* ctx, int graph_id, float* ms_out, int cap, int* n_ou
 
 int tg_debug_gemm_error(int reset) { return tg::gemm_tc_error_flag(reset != 0); }
 int tg_debug_gemm_dbg(int* out8) { return tg::gemm_tc_debug(out8); }
+int tg_debug_gemm_trace(long long* out, int cap) { return tg::gemm_tc_trace(out, cap); }
 
 const char* tg_last_error_name(void) { return g_err_name.c_str(); }
 const char* tg_last_error_message(void) { return g_err_msg.c_str(); }

@@ -146,6 +146,7 @@ bool launch_gemm_tc(const GemmDesc& g, cudaStream_t s);
 // Error code a tcgen05 GEMM recorded after a bounded wait ran out (0 = none).
 int gemm_tc_error_flag(bool reset);
 int gemm_tc_debug(int* out8);
+int gemm_tc_trace(long long* out, int cap);
 
 // Embedding gather: out[r, :] = table[idx[r], :] (0 where idx out of range).
 void launch_gather_rows(const int* idx, const float* table, float* out, int64_t rows, int64_t V,

@@ -50,6 +50,12 @@ __device__ int g_gemm_tc_error = 0;
 // [0] producer stages issued, [1] stages split, [2] MMA stages issued,
 // [3] epilogue reached.
 __device__ int g_gemm_tc_dbg[8];
+// Pipeline timeline of CTA (0,0,0) when TcParams::trace is set (SM clock
+// cycles): [0][it] TMA issued, [1][it] stage landed (split warps),
+// [2][it] split done, [3][it] MMAs issued, [4][c] chunk drained,
+// [5][0] start, [5][1] epilogue start, [5][2] epilogue end.
+constexpr int TC_TRACE_N = 64;
+__device__ long long g_gemm_tc_trace[6][TC_TRACE_N];
 
 constexpr int TC_BM = 128, TC_BN = 128, TC_BK = 32, TC_STAGES = 3;
 constexpr int TC_TILE_BYTES = 128 * TC_BK * 4;  // 16 KB per operand tile
@@ -76,6 +82,8 @@ struct TcParams {
   int accumulate;
   int splits, kps;  // split-K: number of K ranges and K-stages per range
   float* ws;        // [splits][batch][M][N] partial tiles when splits > 1
+  int trace;        // record the pipeline timeline of CTA (0,0,0)
+  int tma_store;    // write the tile with TMA stores through tmC (else plain stores)
 };
 
 // ------------------------------------------------------------- PTX helpers --
@@ -111,6 +119,11 @@ __device__ __forceinline__ void tma_load_4d(const CUtensorMap* tm, uint64_t* bar
       "cp.async.bulk.tensor.4d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4, %5}], [%6];"
       ::"r"(smem_u32(dst)), "l"(tm), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(smem_u32(bar))
       : "memory");
+}
+__device__ __forceinline__ void tma_store_4d(const CUtensorMap* tm, const void* src, int c0, int c1, int c2, int c3) {
+  asm volatile("cp.async.bulk.tensor.4d.global.shared::cta.bulk_group [%0, {%1, %2, %3, %4}], [%5];"
+               ::"l"(tm), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(smem_u32(src))
+               : "memory");
 }
 __device__ __forceinline__ uint64_t umma_desc(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
   uint64_t d = 0;
@@ -247,9 +260,13 @@ __device__ __forceinline__ void split_b(uint8_t* st, int t, bool kmajor) {
 
 __global__ void __launch_bounds__(192, 1) gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA,
                                                          const __grid_constant__ CUtensorMap tmB,
+                                                         const __grid_constant__ CUtensorMap tmC,
                                                          const __grid_constant__ TcParams P) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  // 1 KB-aligned base for the 128B-swizzled tiles. Offsetting the shared
+  // array (rather than casting through an integer) keeps the pointer in the
+  // shared address space, so tile accesses compile to shared loads/stores.
+  uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + TC_STAGES * TC_STAGE_BYTES);
   uint64_t* conv = full + TC_STAGES;
   uint64_t* empty = conv + TC_STAGES;
@@ -268,6 +285,10 @@ __global__ void __launch_bounds__(192, 1) gemm_tc_kernel(const __grid_constant__
   const int nchunks = (nk + TC_CHUNK - 1) / TC_CHUNK;
   const bool first_cta = blockIdx.x == 0 && blockIdx.y == 0 && blockIdx.z == 0;
   const bool partial = P.splits > 1;
+  const bool tr = P.trace && first_cta;
+  auto mark = [&](int row, int i) {
+    if (tr && i < TC_TRACE_N) g_gemm_tc_trace[row][i] = clock64();
+  };
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < TC_STAGES; ++s) {
@@ -290,6 +311,7 @@ __global__ void __launch_bounds__(192, 1) gemm_tc_kernel(const __grid_constant__
   asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
   const uint32_t tmem = *tmem_slot;
   bool ok = true;
+  if (threadIdx.x == 0) mark(5, 0);
 
   if (warp == 0) {
     // ---------------------------------------------------------- producer --
@@ -301,6 +323,7 @@ __global__ void __launch_bounds__(192, 1) gemm_tc_kernel(const __grid_constant__
         const uint32_t ph = (uint32_t)(it / TC_STAGES) & 1u;
         if (it >= TC_STAGES && !mbar_wait(&empty[s], ph ^ 1u, 1)) { ok = false; break; }
         uint8_t* st = smem + s * TC_STAGE_BYTES;
+        mark(0, it);
         mbar_expect_tx(&full[s], 2 * TC_TILE_BYTES);
         const int k0 = (kbeg + it) * TC_BK;
         if (P.a_kmajor) tma_load_4d(&tmA, &full[s], st, k0, (int)m0, ab1, ab2);
@@ -342,6 +365,7 @@ __global__ void __launch_bounds__(192, 1) gemm_tc_kernel(const __grid_constant__
           umma_tf32_ts(dacc, a_hi + kk * 8, dBl, idesc, 1u);
           umma_tf32_ts(dacc, a_hi + kk * 8, dBh, idesc, 1u);
         }
+        mark(3, it);
         umma_commit(&empty[s]);  // frees the stage (smem and TMEM A) once these MMAs have read it
         if ((it % TC_CHUNK) == TC_CHUNK - 1 || it == nk - 1) umma_commit(&dfull[acc]);
         if (first_cta) g_gemm_tc_dbg[2] = it + 1;
@@ -371,12 +395,14 @@ __global__ void __launch_bounds__(192, 1) gemm_tc_kernel(const __grid_constant__
       }
       asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
       mbar_arrive(&dempty[acc]);
+      if (t == 0) mark(4, c);
       return true;
     };
     for (int it = 0; it < nk && ok; ++it) {
       const int s = it % TC_STAGES;
       const uint32_t ph = (uint32_t)(it / TC_STAGES) & 1u;
       if (!mbar_wait(&full[s], ph, 3)) { ok = false; break; }
+      if (t == 0) mark(1, it);
       uint8_t* st = smem + s * TC_STAGE_BYTES;
       split_a_row(st, r, P.a_kmajor != 0, tmem + lane_base + TC_ACOL + 64u * (uint32_t)s);
       split_b(st, t, P.b_kmajor != 0);
@@ -384,6 +410,7 @@ __global__ void __launch_bounds__(192, 1) gemm_tc_kernel(const __grid_constant__
       asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
       asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
       mbar_arrive(&conv[s]);
+      if (t == 0) mark(2, it);
       if (t == 0 && first_cta) g_gemm_tc_dbg[1] = it + 1;
       // after splitting the last stage of chunk c+1, drain chunk c
       if ((it % TC_CHUNK) == TC_CHUNK - 1 && it / TC_CHUNK >= 1) {
@@ -395,63 +422,149 @@ __global__ void __launch_bounds__(192, 1) gemm_tc_kernel(const __grid_constant__
       if (!drain(drained)) { ok = false; break; }
       ++drained;
     }
-    if (ok) {
-      if (t == 0 && first_cta) g_gemm_tc_dbg[3] = 1;
-      const int64_t row = m0 + r;
-      // split-K: raw partial tile into the workspace, finished by gemm_splitk_reduce
-      float* C = partial ? P.ws + ((int64_t)sp * P.batch + zb) * P.M * P.N
-                         : P.C + (int64_t)i1 * P.c_batch + (int64_t)i2 * P.c_batch2;
-      const int64_t cm = partial ? P.N : P.c_m, cn = partial ? 1 : P.c_n;
-      const float alpha = partial ? 1.f : P.alpha;
-      const float* bias = partial ? nullptr : P.bias;
-      const bool bias_m = P.bias_m != 0;
-      const int accumulate = partial ? 0 : P.accumulate;
-      if (row < P.M) {
-        const float brow = (bias && bias_m) ? bias[row] : 0.f;
-        const float* bcol = (bias && !bias_m) ? bias : nullptr;
+    // ------------------------------------------------------------ epilogue --
+    // The finished tile goes through shared memory (every stage is free: the
+    // last drain waited for the final MMAs), so that each warp then writes
+    // whole 512-byte lines of C with float4 stores: tile rows when C is
+    // row-major, tile columns when it is column-major (after an operand swap).
+    if (t == 0 && first_cta && ok) g_gemm_tc_dbg[3] = 1;
+    if (t == 0) mark(5, 1);
+    float* C = partial ? P.ws + ((int64_t)sp * P.batch + zb) * P.M * P.N
+                       : P.C + (int64_t)i1 * P.c_batch + (int64_t)i2 * P.c_batch2;
+    const int64_t cm = partial ? P.N : P.c_m, cn = partial ? 1 : P.c_n;
+    const float alpha = partial ? 1.f : P.alpha;
+    const float* bias = partial ? nullptr : P.bias;
+    const bool bias_m = P.bias_m != 0;
+    const bool accumulate = !partial && P.accumulate;
+    const bool colmaj = cm == 1 && cn != 1;
+    constexpr int LD = TC_BN + 4;  // padded line: conflict-free float4 and scalar staging
+    float* T = reinterpret_cast<float*>(smem);
+    if (P.tma_store) {
+      // Four 128B-swizzled sub-tiles of 32 lines x 128 elements (the operand
+      // tile layout), stored by TMA; the hardware clips ragged edges. Lines
+      // are tile rows for row-major C and tile columns for column-major C.
+      if (ok) {
+        const float brow = (bias && bias_m && m0 + r < P.M) ? bias[m0 + r] : 0.f;
+        if (!colmaj) {
 #pragma unroll
-        for (int q = 0; q < TC_BN / 32; ++q) {
-          const int64_t col0 = n0 + q * 32;
-          if (col0 >= P.N) break;
-          if (cn == 1) {
-            float* dst = C + row * cm + col0;
-            const bool vec = (col0 + 32 <= P.N) && ((cm & 3) == 0) && ((reinterpret_cast<uintptr_t>(dst) & 15) == 0);
-            if (vec) {
+          for (int j = 0; j < 4; ++j) {
 #pragma unroll
-              for (int j = 0; j < 32; j += 4) {
-                float4 v = make_float4(sum[q * 32 + j] * alpha + brow, sum[q * 32 + j + 1] * alpha + brow,
-                                       sum[q * 32 + j + 2] * alpha + brow, sum[q * 32 + j + 3] * alpha + brow);
-                if (bcol) {
-                  v.x += bcol[col0 + j]; v.y += bcol[col0 + j + 1];
-                  v.z += bcol[col0 + j + 2]; v.w += bcol[col0 + j + 3];
-                }
-                float4* d4 = reinterpret_cast<float4*>(dst + j);
-                if (accumulate) {
-                  const float4 o = *d4;
-                  v.x += o.x; v.y += o.y; v.z += o.z; v.w += o.w;
-                }
-                *d4 = v;
+            for (int c = 0; c < 8; ++c) {
+              float v[4];
+#pragma unroll
+              for (int e = 0; e < 4; ++e) {
+                const int n = 32 * j + 4 * c + e;
+                v[e] = sum[n] * alpha + brow;
+                if (bias && !bias_m && n0 + n < P.N) v[e] += bias[n0 + n];
               }
-              continue;
+              *reinterpret_cast<float4*>(smem + j * TC_TILE_BYTES + r * 128 + ((c ^ (r & 7)) << 4)) =
+                  make_float4(v[0], v[1], v[2], v[3]);
             }
           }
-          // general strides; with c_m == 1 (swapped operands) the 32 lanes
-          // write 32 consecutive floats per column
+        } else {
+          uint8_t* sub = smem + (r >> 5) * TC_TILE_BYTES + ((r & 3) << 2);
+          const int mc = (r & 31) >> 2;
 #pragma unroll
-          for (int j = 0; j < 32; ++j) {
-            const int64_t col = col0 + j;
-            if (col < P.N) {
-              float v = sum[q * 32 + j] * alpha + brow;
-              if (bcol) v += bcol[col];
-              float* d = C + row * cm + col * cn;
-              if (accumulate) v += *d;
-              *d = v;
+          for (int n = 0; n < TC_BN; ++n) {
+            float v = sum[n] * alpha + brow;
+            if (bias && !bias_m && n0 + n < P.N) v += bias[n0 + n];
+            *reinterpret_cast<float*>(sub + n * 128 + ((mc ^ (n & 7)) << 4)) = v;
+          }
+        }
+      }
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      asm volatile("bar.sync 1, 128;" ::: "memory");
+      if (t == 0 && ok) {
+        const int z2 = partial ? sp * (int)P.batch + (int)zb : i1;
+        const int z3 = partial ? 0 : i2;
+        const int64_t inner0 = colmaj ? m0 : n0, inner_n = colmaj ? P.M : P.N;
+        const int outer0 = (int)(colmaj ? n0 : m0);
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+          if (inner0 + 32 * j < inner_n)
+            tma_store_4d(&tmC, smem + j * TC_TILE_BYTES, (int)(inner0 + 32 * j), outer0, z2, z3);
+        asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+        asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+      }
+    } else if (cn == 1 || cm == 1) {
+      if (ok) {
+        if (!colmaj) {
+#pragma unroll
+          for (int q = 0; q < TC_BN / 4; ++q)
+            *reinterpret_cast<float4*>(T + r * LD + 4 * q) =
+                make_float4(sum[4 * q], sum[4 * q + 1], sum[4 * q + 2], sum[4 * q + 3]);
+        } else {
+#pragma unroll
+          for (int j = 0; j < TC_BN; ++j) T[j * LD + r] = sum[j];
+        }
+      }
+      if (t == 0) mark(5, 3);
+      asm volatile("bar.sync 1, 128;" ::: "memory");
+      if (t == 0) mark(5, 4);
+      // line = tile row (row-major C) or tile column (column-major C)
+      const int64_t rows_left = P.M - m0 < TC_BM ? P.M - m0 : TC_BM;
+      const int64_t cols_left = P.N - n0 < TC_BN ? P.N - n0 : TC_BN;
+      const int64_t nlines = colmaj ? cols_left : rows_left;
+      const int64_t nelem = colmaj ? rows_left : cols_left;
+      const int e0 = lane * 4;
+      const bool by_line = colmaj != bias_m;  // bias follows n: the line (column-major C) or the element
+      const int64_t bbase = bias_m ? m0 : n0;
+      // 8 lines in flight per warp: all shared loads, then all global stores
+#pragma unroll 1
+      for (int i0 = 0; ok && i0 < TC_BM / 4; i0 += 8) {
+        float4 x[8];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+          const int ln = g + 4 * (i0 + u);
+          x[u] = ln < nlines ? *reinterpret_cast<const float4*>(T + ln * LD + e0) : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+          const int ln = g + 4 * (i0 + u);
+          if (ln >= nlines) break;
+          float* lp = colmaj ? C + (n0 + ln) * cn + m0 : C + (m0 + ln) * cm + n0;
+          float v[4] = {x[u].x * alpha, x[u].y * alpha, x[u].z * alpha, x[u].w * alpha};
+          if (bias) {
+#pragma unroll
+            for (int e = 0; e < 4; ++e)
+              if (by_line || e0 + e < nelem) v[e] += bias[bbase + (by_line ? ln : e0 + e)];
+          }
+          if (e0 + 3 < nelem && ((reinterpret_cast<uintptr_t>(lp + e0) & 15) == 0)) {
+            float4* d4 = reinterpret_cast<float4*>(lp + e0);
+            if (accumulate) {
+              const float4 o = *d4;
+              v[0] += o.x; v[1] += o.y; v[2] += o.z; v[3] += o.w;
             }
+            *d4 = make_float4(v[0], v[1], v[2], v[3]);
+          } else {
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              if (e0 + e < nelem) {
+                float* d = lp + e0 + e;
+                *d = accumulate ? *d + v[e] : v[e];
+              }
+            }
+          }
+        }
+      }
+    } else if (ok) {
+      // neither stride is 1: element by element from registers
+      const int64_t row = m0 + r;
+      if (row < P.M) {
+#pragma unroll
+        for (int j = 0; j < TC_BN; ++j) {
+          const int64_t col = n0 + j;
+          if (col < P.N) {
+            float v = sum[j] * alpha;
+            if (bias) v += bias[bias_m ? row : col];
+            float* d = C + row * cm + col * cn;
+            *d = accumulate ? *d + v : v;
           }
         }
       }
     }
   }
+  if (threadIdx.x == 64) mark(5, 2);
   __syncthreads();
   if (warp == 1) {
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
@@ -595,6 +708,20 @@ bool launch_gemm_tc(const GemmDesc& g, cudaStream_t s) {
   splits = (int)((nk + p.kps - 1) / p.kps);  // every split gets at least one K-stage
   p.splits = splits;
   p.ws = g.workspace;
+  static const int trace = [] { const char* e = getenv("TG_GEMM_TRACE"); return e && e[0] == '1' ? 1 : 0; }();
+  p.trace = trace;
+  // Output tensor map (row-major tiles {32 inner, 128 outer}); plain stores
+  // when C's layout is not TMA-describable or the result accumulates.
+  CUtensorMap tc;
+  memset(&tc, 0, sizeof tc);
+  if (splits > 1) {
+    p.tma_store = make_map(&tc, g.workspace, true, M, N, N, 1, (int64_t)splits * g.batch, M * N, 1, 0) ? 1 : 0;
+  } else if (!g.accumulate && (c_n == 1 || c_m == 1)) {
+    const bool cmaj = c_m == 1 && c_n != 1;
+    const int64_t inner = cmaj ? M : N, outer = cmaj ? N : M, ld = cmaj ? c_n : c_m;
+    p.tma_store = make_map(&tc, g.C, true, outer, inner, ld, 1, g.c_batch ? b1 : 1, g.c_batch,
+                           g.c_batch2 ? b2 : 1, g.c_batch2) ? 1 : 0;
+  }
 
   static bool attr = false;
   if (!attr) {
@@ -603,7 +730,7 @@ bool launch_gemm_tc(const GemmDesc& g, cudaStream_t s) {
     attr = true;
   }
   dim3 grid((unsigned)((N + TC_BN - 1) / TC_BN), (unsigned)((M + TC_BM - 1) / TC_BM), (unsigned)(g.batch * splits));
-  gemm_tc_kernel<<<grid, 192, TC_SMEM, s>>>(ta, tb, p);
+  gemm_tc_kernel<<<grid, 192, TC_SMEM, s>>>(ta, tb, tc, p);
   if (splits > 1) {
     int64_t total = g.batch * M * N;
     int64_t blocks = (total + 255) / 256, cap = (int64_t)device_sm_count() * 8;
@@ -614,6 +741,12 @@ bool launch_gemm_tc(const GemmDesc& g, cudaStream_t s) {
 
 int gemm_tc_debug(int* out8) {
   return cudaMemcpyFromSymbol(out8, g_gemm_tc_dbg, 8 * sizeof(int)) == cudaSuccess ? 0 : 1;
+}
+
+int gemm_tc_trace(long long* out, int cap) {
+  const int n = 6 * TC_TRACE_N;
+  if (cap < n) return -1;
+  return cudaMemcpyFromSymbol(out, g_gemm_tc_trace, n * sizeof(long long)) == cudaSuccess ? n : -1;
 }
 
 int gemm_tc_error_flag(bool reset) {
