@@ -136,8 +136,8 @@ static int64_t scratch_for(const Program& P, int i, int action) {
   }
   if (k == "sum_to_shape") {
     int a = P.op(i)["a"].i32();
-    int64_t inner = P.T[P.out[i]].numel;
-    return (int64_t)colsum_scratch_floats(P.T[a].numel / std::max<int64_t>(inner, 1), inner) * 4;
+    int64_t inner = P.T[P.out[i]].numel, outer = P.T[a].numel / std::max<int64_t>(inner, 1);
+    return (int64_t)std::max(colsum_scratch_floats(outer, inner), row_scratch_floats(ROW_SUM, inner, outer)) * 4;
   }
   return 0;
 }
@@ -664,6 +664,20 @@ void Graph::emit_launches() {
       bool suffix = true;
       bool seen_keep = false;
       for (int d = 0; d < R; ++d) { if (keep[d]) seen_keep = true; else if (seen_keep && is[d] != 1) suffix = false; }
+      // kept dims all before the reduced ones: a row sum over the trailing extent
+      bool prefix = true;
+      bool seen_red = false;
+      for (int d = 0; d < R; ++d) {
+        if (is[d] == 1) continue;
+        if (!keep[d]) seen_red = true; else if (seen_red) prefix = false;
+      }
+      if (prefix && !suffix) {
+        const float* x = reinterpret_cast<const float*>(ptr(a));
+        float* out = reinterpret_cast<float*>(ptr(o));
+        int64_t rows = P.T[o].numel, D = P.T[a].numel / std::max<int64_t>(rows, 1);
+        add("rowsum", [=](cudaStream_t s) { launch_row(ROW_SUM, x, out, rows, D, s, nullptr, 0, scratch, scratch_floats); });
+        continue;
+      }
       const float* x = reinterpret_cast<const float*>(ptr(a));
       float* out = reinterpret_cast<float*>(ptr(o));
       int64_t inner = P.T[o].numel, outer = P.T[a].numel / std::max<int64_t>(inner, 1);

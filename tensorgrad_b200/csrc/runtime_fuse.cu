@@ -9,7 +9,8 @@
 //   * has exactly one consumer (this op) and no view of it is taken,
 //   * is not observable from the host (loss, output, capture, gradient,
 //     writeback source),
-//   * has the consumer's output shape, so both index it the same way, and
+//   * has the consumer's output shape, or broadcasts to it and contains no
+//     position-dependent op (its value is then recomputed per element), and
 //   * sits on the same side of the optimizer section.
 // The absorbed tensors get no storage. Each group is written out as CUDA C
 // with shapes, strides and constants as literals (dims divide by constants,
@@ -73,6 +74,15 @@ std::string lit(float f) {
   return buf;
 }
 
+// Right-aligned broadcast of shape a onto shape b.
+bool broadcasts_to(const std::vector<int64_t>& a, const std::vector<int64_t>& b) {
+  if (a.size() > b.size()) return false;
+  const size_t off = b.size() - a.size();
+  for (size_t d = 0; d < a.size(); ++d)
+    if (a[d] != 1 && a[d] != b[off + d]) return false;
+  return true;
+}
+
 constexpr int kMaxGroupInputs = 12;
 constexpr int kMaxGroupOps = 48;
 
@@ -100,6 +110,8 @@ void Graph::plan_fusion() {
 
   std::vector<std::vector<int>> members(nO);
   std::vector<std::set<int>> ext(nO);  // tensors a group reads from memory
+  std::vector<char> posdep(nO, 0);     // group uses the element index (dropout, causal mask)
+  for (int i = 0; i < nO; ++i) posdep[i] = P.kind[i] == "dropout" || P.kind[i] == "where_causal";
   auto side = [&](int i) { return P.opt_start >= 0 && i >= P.opt_start; };
   for (int i = 0; i < nO; ++i) {
     if (ew_root_[i] != i) continue;
@@ -115,13 +127,19 @@ void Graph::plan_fusion() {
       if (observable.count(t)) continue;
       const TView& v = views_[t];
       if (v.root != t || v.onehot || !v.contiguous) continue;
-      if (P.T[t].shape != P.T[P.out[i]].shape) continue;
+      if (P.T[t].shape != P.T[P.out[i]].shape) {
+        // a smaller producer whose value the consumer reads broadcast is
+        // recomputed per output element; exact for pure elementwise ops, but
+        // not for ones that use the element's position
+        if (!broadcasts_to(P.T[t].shape, P.T[P.out[i]].shape) || posdep[p]) continue;
+      }
       if (side(p) != side(i)) continue;
       std::set<int> merged = ext[i];
       merged.erase(t);
       merged.insert(ext[p].begin(), ext[p].end());
       if ((int)merged.size() > kMaxGroupInputs) continue;
       if ((int)(members[i].size() + members[p].size()) > kMaxGroupOps) continue;
+      posdep[i] = posdep[i] || posdep[p];
       for (int m : members[p]) ew_root_[m] = i;
       members[i].insert(members[i].end(), members[p].begin(), members[p].end());
       members[p].clear();

@@ -57,3 +57,11 @@ def test_gemm_split_k_batched(ctx):
     a = rnd([3, 64, 2048], 46)
     b = rnd([3, 2048, 96], 47)
     run(ctx, lambda: tg.matmul(T("a", [3, 64, 2048]), T("b", [3, 2048, 96])), {"a": a, "b": b})
+
+
+def test_gemm_simt_split_k_unaligned(ctx):
+    """65-wide rows (not 16-byte aligned, so not TMA-describable) with a long
+    K: the CUDA-core kernel splits K and sums the partial tiles in order."""
+    x = rnd([8192, 96], 48)
+    dy = rnd([8192, 65], 49)
+    run(ctx, lambda: tg.matmul(tg.swapAxes(T("x", [8192, 96]), 0, 1), T("dy", [8192, 65])), {"x": x, "dy": dy})

@@ -147,6 +147,15 @@ def test_layout_ops(ctx):
     run(ctx, lambda: tg.sumToShape(T("a", [3, 4, 5, 6]), [4, 1, 6]), {"a": a})
 
 
+def test_sum_to_shape_trailing(ctx):
+    """Kept leading dims, reduced trailing dims: the row-sum path (LayerNorm
+    backward shape), including a long row that splits across blocks."""
+    a = rnd([64, 33, 384], 61)
+    run(ctx, lambda: tg.sumToShape(T("a", [64, 33, 384]), [64, 33, 1]), {"a": a})
+    b = rnd([3, 40000], 62)
+    run(ctx, lambda: tg.sumToShape(T("b", [3, 40000]), [3, 1]), {"b": b})
+
+
 @pytest.mark.parametrize("M,K,N", [(1, 1, 1), (37, 29, 53), (256, 384, 200), (130, 1, 70)])
 def test_matmul_2d(ctx, M, K, N):
     run(ctx, lambda: tg.matmul(T("a", [M, K]), T("b", [K, N])), {"a": rnd([M, K], 21), "b": rnd([K, N], 22)})
