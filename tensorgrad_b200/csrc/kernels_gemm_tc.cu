@@ -46,7 +46,7 @@
 namespace tg {
 
 __device__ int g_gemm_tc_error = 0;
-// Progress markers of CTA (0,0,0) for diagnosing a stalled pipeline:
+// Progress markers of CTA 0 for diagnosing a stalled pipeline:
 // [0] producer stages issued, [1] stages split, [2] MMA stages issued,
 // [3] epilogue reached.
 __device__ int g_gemm_tc_dbg[8];
@@ -63,7 +63,8 @@ constexpr int TC_TILE_BYTES = 128 * TC_BK * 4;  // 16 KB per operand tile
 // a K-major B here and it is split in place), [2] B lo, [3] B as landed when
 // it is MN-major.
 constexpr int TC_STAGE_BYTES = 4 * TC_TILE_BYTES;
-constexpr int TC_SMEM = TC_STAGES * TC_STAGE_BYTES + 1024 + 256;
+constexpr int TC_EPI_BYTES = 2 * TC_TILE_BYTES;  // output staging: half a tile at a time
+constexpr int TC_SMEM = TC_STAGES * TC_STAGE_BYTES + TC_EPI_BYTES + 1024 + 256;
 constexpr uint32_t TC_TMEM_COLS = 512;
 constexpr uint32_t TC_ACOL = 2 * TC_BN;  // first TMEM column of the per-stage A hi/lo (64 columns each)
 constexpr long long TC_SPIN_LIMIT = 1ll << 22;
@@ -84,6 +85,7 @@ struct TcParams {
   float* ws;        // [splits][batch][M][N] partial tiles when splits > 1
   int trace;        // record the pipeline timeline of CTA (0,0,0)
   int tma_store;    // write the tile with TMA stores through tmC (else plain stores)
+  int64_t units;    // output tiles x batch x K ranges
 };
 
 // ------------------------------------------------------------- PTX helpers --
@@ -158,6 +160,13 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
         "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
       : "r"(taddr));
 }
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+}
 // One warp writes 16 consecutive 32-bit columns of its 32 TMEM lanes.
 __device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&v)[16]) {
   asm volatile(
@@ -173,10 +182,32 @@ __device__ __forceinline__ float tf32_hi(float x) { return __uint_as_float(__flo
 // Accumulator chunking: the tensor core accumulates in f32 without
 // round-to-nearest on every add, so error grows with the number of
 // accumulation steps. The MMA warp therefore alternates between two TMEM
-// accumulators every TC_CHUNK K-stages (128 MMA-K), and the split/epilogue
-// warps drain each finished accumulator into per-thread f32 registers with
+// accumulators every TC_CHUNK K-stages (128 MMA-K), and the epilogue warps
+// drain each finished accumulator into per-thread f32 registers with
 // round-to-nearest adds; total error then grows like sqrt(K) instead of K.
 constexpr int TC_CHUNK = 4;
+
+// One output tile of one batch entry and one K range: the persistent CTAs'
+// unit of work, numbered with the N tile fastest.
+struct TcUnit {
+  int64_t m0, n0, zb;
+  int sp, i1, i2, kbeg, nk;
+};
+__device__ __forceinline__ TcUnit tc_unit(const TcParams& P, int64_t u) {
+  const int64_t tn = (P.N + TC_BN - 1) / TC_BN, tm = (P.M + TC_BM - 1) / TC_BM;
+  const int64_t z = u / (tm * tn), rem = u % (tm * tn);
+  TcUnit U;
+  U.m0 = (rem / tn) * TC_BM;
+  U.n0 = (rem % tn) * TC_BN;
+  U.zb = z / P.splits;
+  U.sp = (int)(z % P.splits);
+  U.i1 = (int)(U.zb / P.batch2);
+  U.i2 = (int)(U.zb % P.batch2);
+  const int nk_all = (int)((P.K + TC_BK - 1) / TC_BK);
+  U.kbeg = U.sp * P.kps;
+  U.nk = max(0, min(nk_all, U.kbeg + P.kps) - U.kbeg);
+  return U;
+}
 
 // A tile row r (this thread's TMEM lane) -> hi/lo columns of the stage.
 // K-major landing: row r is 128 bytes, 16-byte chunk c stored at c ^ (r % 8).
@@ -204,15 +235,13 @@ __device__ __forceinline__ void split_a_row(const uint8_t* a, int r, bool kmajor
         v[kk] = *reinterpret_cast<const float*>(box + k * 128 + ((((m >> 2) ^ (k & 7))) << 4) + ((m & 3) << 2));
       }
     }
-    uint32_t hi[16], lo[16];
+    uint32_t w[16];
 #pragma unroll
-    for (int e = 0; e < 16; ++e) {
-      const float hh = tf32_hi(v[e]);
-      hi[e] = __float_as_uint(hh);
-      lo[e] = __float_as_uint(v[e] - hh);
-    }
-    tmem_st16(tcol + 16 * h, hi);
-    tmem_st16(tcol + 32 + 16 * h, lo);
+    for (int e = 0; e < 16; ++e) w[e] = __float_as_uint(tf32_hi(v[e]));
+    tmem_st16(tcol + 16 * h, w);
+#pragma unroll
+    for (int e = 0; e < 16; ++e) w[e] = __float_as_uint(v[e] - __uint_as_float(w[e]));
+    tmem_st16(tcol + 32 + 16 * h, w);
   }
 }
 
@@ -234,31 +263,46 @@ __device__ __forceinline__ void split_b(uint8_t* st, int t, bool kmajor) {
       lo[q] = l;
     }
   } else {
-    // landed MN-major in slot 3: 4 boxes (N chunk j) of 32 K-rows x 128
-    // bytes; element (k, n) sits in row k, 16-byte chunk (n%32)/4 XOR (k%8).
-    // Write hi/lo transposed: element (n, k) in row n, chunk (k/4) XOR (n%8).
+    // Landed MN-major in slot 3: 4 boxes (N chunk j) of 32 K-rows x 128
+    // bytes; element (k, n) sits in row k, chunk (n%32)/4 XOR (k%8). Each
+    // item is a 4(K) x 4(N) block: four 16-byte row reads, a register
+    // transpose, four 16-byte writes each to hi and lo, where element (n, k)
+    // sits in row n, chunk (k/4) XOR (n%8). Lanes of a quarter-warp take two
+    // N chunks x four K quads: the writes are conflict-free, the reads 2-way.
     const uint8_t* stg = st + 3 * TC_TILE_BYTES;
-#pragma unroll 2
-    for (int q = t; q < TC_TILE_BYTES / 16; q += 128) {
-      const int j = q >> 8;
-      const int k = (q >> 3) & 31;
-      const int pc = q & 7;
-      const int lc = pc ^ (k & 7);
-      const float4 x = *reinterpret_cast<const float4*>(stg + q * 16);
-      const float* xv = &x.x;
+    const int l8 = t & 7, q = (t >> 3) & 3, wq = t >> 5;
 #pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const int n = j * 32 + lc * 4 + e;
-        const uint32_t o = (uint32_t)n * 128u + (uint32_t)((((k >> 2) ^ (n & 7)) << 4) + ((k & 3) << 2));
-        const float hh = tf32_hi(xv[e]);
-        *reinterpret_cast<float*>(hi_t + o) = hh;
-        *reinterpret_cast<float*>(lo_t + o) = xv[e] - hh;
+    for (int it2 = 0; it2 < 2; ++it2) {
+      const int R = (wq * 4 + q) * 2 + it2;  // 0..31
+      const int c = (R & 3) * 2 + (l8 & 1);
+      const int kq = ((R >> 2) & 1) * 4 + (l8 >> 1);
+      const int j = R >> 3;
+      const uint8_t* box = stg + j * 4096;
+      float v[4][4];
+#pragma unroll
+      for (int kk = 0; kk < 4; ++kk) {
+        const int k = 4 * kq + kk;
+        const float4 x = *reinterpret_cast<const float4*>(box + k * 128 + ((c ^ (k & 7)) << 4));
+        v[kk][0] = x.x; v[kk][1] = x.y; v[kk][2] = x.z; v[kk][3] = x.w;
+      }
+#pragma unroll
+      for (int nn = 0; nn < 4; ++nn) {
+        const int n = 32 * j + 4 * c + nn;
+        const uint32_t o = (uint32_t)n * 128u + (uint32_t)((kq ^ (n & 7)) << 4);
+        float4 h, l;
+        h.x = tf32_hi(v[0][nn]); h.y = tf32_hi(v[1][nn]); h.z = tf32_hi(v[2][nn]); h.w = tf32_hi(v[3][nn]);
+        l.x = v[0][nn] - h.x; l.y = v[1][nn] - h.y; l.z = v[2][nn] - h.z; l.w = v[3][nn] - h.w;
+        *reinterpret_cast<float4*>(hi_t + o) = h;
+        *reinterpret_cast<float4*>(lo_t + o) = l;
       }
     }
   }
 }
 
-__global__ void __launch_bounds__(192, 1) gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA,
+// Persistent: each CTA walks units blockIdx.x, blockIdx.x + gridDim.x, ...;
+// the stage ring, the accumulator pair and every barrier phase continue
+// across units, so one unit's epilogue overlaps the next unit's main loop.
+__global__ void __launch_bounds__(448, 1) gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA,
                                                          const __grid_constant__ CUtensorMap tmB,
                                                          const __grid_constant__ CUtensorMap tmC,
                                                          const __grid_constant__ TcParams P) {
@@ -267,25 +311,17 @@ __global__ void __launch_bounds__(192, 1) gemm_tc_kernel(const __grid_constant__
   // array (rather than casting through an integer) keeps the pointer in the
   // shared address space, so tile accesses compile to shared loads/stores.
   uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + TC_STAGES * TC_STAGE_BYTES);
+  uint8_t* epi = smem + TC_STAGES * TC_STAGE_BYTES;  // two output sub-tiles
+  uint64_t* full = reinterpret_cast<uint64_t*>(epi + TC_EPI_BYTES);
   uint64_t* conv = full + TC_STAGES;
   uint64_t* empty = conv + TC_STAGES;
   uint64_t* dfull = empty + TC_STAGES;   // [2] accumulator chunk finished (MMA commit)
-  uint64_t* dempty = dfull + 2;          // [2] accumulator drained (128 epilogue threads)
+  uint64_t* dempty = dfull + 2;          // [2] accumulator drained (256 epilogue threads)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(dempty + 2);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int64_t n0 = (int64_t)blockIdx.x * TC_BN, m0 = (int64_t)blockIdx.y * TC_BM;
-  const int64_t zb = blockIdx.z / P.splits;   // batch index
-  const int sp = blockIdx.z % P.splits;       // K range
-  const int i1 = (int)(zb / P.batch2), i2 = (int)(zb % P.batch2);
-  const int nk_all = (int)((P.K + TC_BK - 1) / TC_BK);
-  const int kbeg = sp * P.kps;
-  const int nk = max(0, min(nk_all, kbeg + P.kps) - kbeg);
-  const int nchunks = (nk + TC_CHUNK - 1) / TC_CHUNK;
-  const bool first_cta = blockIdx.x == 0 && blockIdx.y == 0 && blockIdx.z == 0;
   const bool partial = P.splits > 1;
-  const bool tr = P.trace && first_cta;
+  const bool tr = P.trace && blockIdx.x == 0;
   auto mark = [&](int row, int i) {
     if (tr && i < TC_TRACE_N) g_gemm_tc_trace[row][i] = clock64();
   };
@@ -298,7 +334,7 @@ __global__ void __launch_bounds__(192, 1) gemm_tc_kernel(const __grid_constant__
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&dfull[a], 1);
-      mbar_init(&dempty[a], 128);
+      mbar_init(&dempty[a], 256);
     }
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
@@ -316,23 +352,27 @@ __global__ void __launch_bounds__(192, 1) gemm_tc_kernel(const __grid_constant__
   if (warp == 0) {
     // ---------------------------------------------------------- producer --
     if (lane == 0) {
-      const int ab1 = P.a_b1 ? i1 : 0, ab2 = P.a_b2 ? i2 : 0;
-      const int bb1 = P.b_b1 ? i1 : 0, bb2 = P.b_b2 ? i2 : 0;
-      for (int it = 0; it < nk && ok; ++it) {
-        const int s = it % TC_STAGES;
-        const uint32_t ph = (uint32_t)(it / TC_STAGES) & 1u;
-        if (it >= TC_STAGES && !mbar_wait(&empty[s], ph ^ 1u, 1)) { ok = false; break; }
-        uint8_t* st = smem + s * TC_STAGE_BYTES;
-        mark(0, it);
-        mbar_expect_tx(&full[s], 2 * TC_TILE_BYTES);
-        const int k0 = (kbeg + it) * TC_BK;
-        if (P.a_kmajor) tma_load_4d(&tmA, &full[s], st, k0, (int)m0, ab1, ab2);
-        else for (int j = 0; j < 4; ++j)
-          tma_load_4d(&tmA, &full[s], st + j * 4096, (int)m0 + 32 * j, k0, ab1, ab2);
-        if (P.b_kmajor) tma_load_4d(&tmB, &full[s], st + TC_TILE_BYTES, k0, (int)n0, bb1, bb2);
-        else for (int j = 0; j < 4; ++j)
-          tma_load_4d(&tmB, &full[s], st + 3 * TC_TILE_BYTES + j * 4096, (int)n0 + 32 * j, k0, bb1, bb2);
-        if (first_cta) g_gemm_tc_dbg[0] = it + 1;
+      int gs = 0;
+      for (int64_t u = blockIdx.x; u < P.units && ok; u += gridDim.x) {
+        const TcUnit U = tc_unit(P, u);
+        const int ab1 = P.a_b1 ? U.i1 : 0, ab2 = P.a_b2 ? U.i2 : 0;
+        const int bb1 = P.b_b1 ? U.i1 : 0, bb2 = P.b_b2 ? U.i2 : 0;
+        for (int it = 0; it < U.nk; ++it, ++gs) {
+          const int s = gs % TC_STAGES;
+          const uint32_t ph = (uint32_t)(gs / TC_STAGES) & 1u;
+          if (gs >= TC_STAGES && !mbar_wait(&empty[s], ph ^ 1u, 1)) { ok = false; break; }
+          uint8_t* st = smem + s * TC_STAGE_BYTES;
+          mark(0, gs);
+          if (blockIdx.x == 0) g_gemm_tc_dbg[0] = gs + 1;
+          mbar_expect_tx(&full[s], 2 * TC_TILE_BYTES);
+          const int k0 = (U.kbeg + it) * TC_BK;
+          if (P.a_kmajor) tma_load_4d(&tmA, &full[s], st, k0, (int)U.m0, ab1, ab2);
+          else for (int j = 0; j < 4; ++j)
+            tma_load_4d(&tmA, &full[s], st + j * 4096, (int)U.m0 + 32 * j, k0, ab1, ab2);
+          if (P.b_kmajor) tma_load_4d(&tmB, &full[s], st + TC_TILE_BYTES, k0, (int)U.n0, bb1, bb2);
+          else for (int j = 0; j < 4; ++j)
+            tma_load_4d(&tmB, &full[s], st + 3 * TC_TILE_BYTES + j * 4096, (int)U.n0 + 32 * j, k0, bb1, bb2);
+        }
       }
     }
   } else if (warp == 1) {
@@ -341,230 +381,190 @@ __global__ void __launch_bounds__(192, 1) gemm_tc_kernel(const __grid_constant__
       // kind::tf32 instruction descriptor: D f32, A/B tf32, K-major, N>>3, M>>4
       const uint32_t idesc = (1u << 4) | (2u << 7) | (2u << 10) | ((uint32_t)(TC_BN >> 3) << 17) |
                              ((uint32_t)(TC_BM >> 4) << 24);
-      for (int it = 0; it < nk && ok; ++it) {
-        const int s = it % TC_STAGES;
-        const uint32_t ph = (uint32_t)(it / TC_STAGES) & 1u;
-        const int chunk = it / TC_CHUNK, acc = chunk & 1;
-        const bool chunk_start = (it % TC_CHUNK) == 0;
-        if (chunk_start && chunk >= 2 && !mbar_wait(&dempty[acc], (uint32_t)((chunk - 2) >> 1) & 1u, 5)) {
-          ok = false; break;
-        }
-        if (!mbar_wait(&conv[s], ph, 2)) { ok = false; break; }
-        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-        const uint32_t base = smem_u32(smem + s * TC_STAGE_BYTES);
-        const uint32_t b_hi = base + TC_TILE_BYTES, b_lo = base + 2 * TC_TILE_BYTES;
-        const uint32_t a_hi = tmem + TC_ACOL + 64u * (uint32_t)s, a_lo = a_hi + 32u;
-        const uint32_t dacc = tmem + (uint32_t)(acc * TC_BN);
+      int gs = 0, gc = 0;
+      for (int64_t u = blockIdx.x; u < P.units && ok; u += gridDim.x) {
+        const TcUnit U = tc_unit(P, u);
+        for (int it = 0; it < U.nk; ++it, ++gs) {
+          const int s = gs % TC_STAGES;
+          const uint32_t ph = (uint32_t)(gs / TC_STAGES) & 1u;
+          const int c = gc + it / TC_CHUNK, acc = c & 1;
+          const bool chunk_start = (it % TC_CHUNK) == 0;
+          if (chunk_start && c >= 2 && !mbar_wait(&dempty[acc], (uint32_t)((c - 2) >> 1) & 1u, 5)) {
+            ok = false; break;
+          }
+          if (!mbar_wait(&conv[s], ph, 2)) { ok = false; break; }
+          asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+          const uint32_t base = smem_u32(smem + s * TC_STAGE_BYTES);
+          const uint32_t b_hi = base + TC_TILE_BYTES, b_lo = base + 2 * TC_TILE_BYTES;
+          const uint32_t a_hi = tmem + TC_ACOL + 64u * (uint32_t)s, a_lo = a_hi + 32u;
+          const uint32_t dacc = tmem + (uint32_t)(acc * TC_BN);
 #pragma unroll
-        for (int kk = 0; kk < TC_BK / 8; ++kk) {
-          // B: 128 rows of 128 bytes (32 K values), 8-row groups 1 KB apart
-          // (SBO); a K step of 8 advances 32 bytes in the row. A: 8 columns.
-          const uint64_t dBh = umma_desc(b_hi + kk * 32, 16, 1024), dBl = umma_desc(b_lo + kk * 32, 16, 1024);
-          const uint32_t first = (chunk_start && kk == 0) ? 0u : 1u;
-          umma_tf32_ts(dacc, a_lo + kk * 8, dBh, idesc, first);
-          umma_tf32_ts(dacc, a_hi + kk * 8, dBl, idesc, 1u);
-          umma_tf32_ts(dacc, a_hi + kk * 8, dBh, idesc, 1u);
+          for (int kk = 0; kk < TC_BK / 8; ++kk) {
+            // B: 128 rows of 128 bytes (32 K values), 8-row groups 1 KB apart
+            // (SBO); a K step of 8 advances 32 bytes in the row. A: 8 columns.
+            const uint64_t dBh = umma_desc(b_hi + kk * 32, 16, 1024), dBl = umma_desc(b_lo + kk * 32, 16, 1024);
+            const uint32_t first = (chunk_start && kk == 0) ? 0u : 1u;
+            umma_tf32_ts(dacc, a_lo + kk * 8, dBh, idesc, first);
+            umma_tf32_ts(dacc, a_hi + kk * 8, dBl, idesc, 1u);
+            umma_tf32_ts(dacc, a_hi + kk * 8, dBh, idesc, 1u);
+          }
+          mark(3, gs);
+          if (blockIdx.x == 0) g_gemm_tc_dbg[2] = gs + 1;
+          umma_commit(&empty[s]);  // frees the stage (smem and TMEM A) once these MMAs have read it
+          if ((it % TC_CHUNK) == TC_CHUNK - 1 || it == U.nk - 1) umma_commit(&dfull[acc]);
         }
-        mark(3, it);
-        umma_commit(&empty[s]);  // frees the stage (smem and TMEM A) once these MMAs have read it
-        if ((it % TC_CHUNK) == TC_CHUNK - 1 || it == nk - 1) umma_commit(&dfull[acc]);
-        if (first_cta) g_gemm_tc_dbg[2] = it + 1;
+        gc += (U.nk + TC_CHUNK - 1) / TC_CHUNK;
+      }
+    }
+  } else if (warp < 6) {
+    // ------------------------------------------------------------- split --
+    const int t = threadIdx.x - 64;  // 0..127
+    const int r = (warp & 3) * 32 + lane;
+    const uint32_t lane_base = (uint32_t)((warp & 3) * 32) << 16;
+    int gs = 0;
+    for (int64_t u = blockIdx.x; u < P.units && ok; u += gridDim.x) {
+      const TcUnit U = tc_unit(P, u);
+      for (int it = 0; it < U.nk; ++it, ++gs) {
+        const int s = gs % TC_STAGES;
+        const uint32_t ph = (uint32_t)(gs / TC_STAGES) & 1u;
+        if (!mbar_wait(&full[s], ph, 3)) { ok = false; break; }
+        if (t == 0) mark(1, gs);
+        uint8_t* st = smem + s * TC_STAGE_BYTES;
+        split_a_row(st, r, P.a_kmajor != 0, tmem + lane_base + TC_ACOL + 64u * (uint32_t)s);
+        split_b(st, t, P.b_kmajor != 0);
+        asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+        mbar_arrive(&conv[s]);
+        if (t == 0) mark(2, gs);
+        if (t == 0 && blockIdx.x == 0) g_gemm_tc_dbg[1] = gs + 1;
       }
     }
   } else {
-    // ---------------------------------------- split, drain, then epilogue --
-    const int t = threadIdx.x - 64;  // 0..127
-    const int g = warp & 3;          // TMEM lane group this warp may access
-    const int r = g * 32 + lane;     // tile row = TMEM lane
-    const uint32_t lane_base = (uint32_t)(g * 32) << 16;
-    float sum[TC_BN];
-#pragma unroll
-    for (int j = 0; j < TC_BN; ++j) sum[j] = 0.f;
-    int drained = 0;
-    auto drain = [&](int c) -> bool {
-      const int acc = c & 1;
-      if (!mbar_wait(&dfull[acc], (uint32_t)(c >> 1) & 1u, 4)) return false;
-      asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-#pragma unroll
-      for (int q = 0; q < TC_BN / 32; ++q) {
-        uint32_t v[32];
-        tmem_ld32(tmem + lane_base + (uint32_t)(acc * TC_BN + q * 32), v);
-        asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-#pragma unroll
-        for (int j = 0; j < 32; ++j) sum[q * 32 + j] += __uint_as_float(v[j]);
-      }
-      asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
-      mbar_arrive(&dempty[acc]);
-      if (t == 0) mark(4, c);
-      return true;
-    };
-    for (int it = 0; it < nk && ok; ++it) {
-      const int s = it % TC_STAGES;
-      const uint32_t ph = (uint32_t)(it / TC_STAGES) & 1u;
-      if (!mbar_wait(&full[s], ph, 3)) { ok = false; break; }
-      if (t == 0) mark(1, it);
-      uint8_t* st = smem + s * TC_STAGE_BYTES;
-      split_a_row(st, r, P.a_kmajor != 0, tmem + lane_base + TC_ACOL + 64u * (uint32_t)s);
-      split_b(st, t, P.b_kmajor != 0);
-      asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
-      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-      asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
-      mbar_arrive(&conv[s]);
-      if (t == 0) mark(2, it);
-      if (t == 0 && first_cta) g_gemm_tc_dbg[1] = it + 1;
-      // after splitting the last stage of chunk c+1, drain chunk c
-      if ((it % TC_CHUNK) == TC_CHUNK - 1 && it / TC_CHUNK >= 1) {
-        if (!drain(drained)) { ok = false; break; }
-        ++drained;
-      }
-    }
-    while (ok && drained < nchunks) {
-      if (!drain(drained)) { ok = false; break; }
-      ++drained;
-    }
-    // ------------------------------------------------------------ epilogue --
-    // The finished tile goes through shared memory (every stage is free: the
-    // last drain waited for the final MMAs), so that each warp then writes
-    // whole 512-byte lines of C with float4 stores: tile rows when C is
-    // row-major, tile columns when it is column-major (after an operand swap).
-    if (t == 0 && first_cta && ok) g_gemm_tc_dbg[3] = 1;
-    if (t == 0) mark(5, 1);
-    float* C = partial ? P.ws + ((int64_t)sp * P.batch + zb) * P.M * P.N
-                       : P.C + (int64_t)i1 * P.c_batch + (int64_t)i2 * P.c_batch2;
-    const int64_t cm = partial ? P.N : P.c_m, cn = partial ? 1 : P.c_n;
+    // ---------------------------------------------------------- epilogue --
+    // Eight warps: two per TMEM lane group, each holding 64 of the tile's 128
+    // columns in registers. Each finished accumulator chunk is drained and
+    // added in f32; the unit's tile is then written in two halves, staged as
+    // 128B-swizzled 32 x 128 sub-tiles and stored by TMA (the hardware clips
+    // ragged edges). Lines are tile rows for row-major C and tile columns for
+    // column-major C. After a failed wait these threads skip the data work but
+    // keep every named barrier.
+    const int e = threadIdx.x - 192;  // 0..255
+    const int r = (warp & 3) * 32 + lane;
+    const int hh = (warp - 6) >> 2;   // column half held in registers
+    const int cb = 64 * hh;
+    const uint32_t lane_base = (uint32_t)((warp & 3) * 32) << 16;
     const float alpha = partial ? 1.f : P.alpha;
     const float* bias = partial ? nullptr : P.bias;
     const bool bias_m = P.bias_m != 0;
-    const bool accumulate = !partial && P.accumulate;
+    const int64_t cm = partial ? P.N : P.c_m, cn = partial ? 1 : P.c_n;
     const bool colmaj = cm == 1 && cn != 1;
-    constexpr int LD = TC_BN + 4;  // padded line: conflict-free float4 and scalar staging
-    float* T = reinterpret_cast<float*>(smem);
-    if (P.tma_store) {
-      // Four 128B-swizzled sub-tiles of 32 lines x 128 elements (the operand
-      // tile layout), stored by TMA; the hardware clips ragged edges. Lines
-      // are tile rows for row-major C and tile columns for column-major C.
-      if (ok) {
-        const float brow = (bias && bias_m && m0 + r < P.M) ? bias[m0 + r] : 0.f;
-        if (!colmaj) {
+    const bool accumulate = !partial && P.accumulate;
+    int gc = 0;
+    for (int64_t u = blockIdx.x; u < P.units; u += gridDim.x) {
+      const TcUnit U = tc_unit(P, u);
+      const int nchunks = (U.nk + TC_CHUNK - 1) / TC_CHUNK;
+      float sum[64];
 #pragma unroll
-          for (int j = 0; j < 4; ++j) {
+      for (int j = 0; j < 64; ++j) sum[j] = 0.f;
+      for (int c = 0; c < nchunks; ++c) {
+        const int g = gc + c, acc = g & 1;
+        if (ok && !mbar_wait(&dfull[acc], (uint32_t)(g >> 1) & 1u, 4)) ok = false;
+        if (ok) {
+          asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
 #pragma unroll
-            for (int c = 0; c < 8; ++c) {
-              float v[4];
+          for (int q = 0; q < 4; ++q) {
+            uint32_t v[16];
+            tmem_ld16(tmem + lane_base + (uint32_t)(acc * TC_BN + cb + q * 16), v);
+            asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 #pragma unroll
-              for (int e = 0; e < 4; ++e) {
-                const int n = 32 * j + 4 * c + e;
-                v[e] = sum[n] * alpha + brow;
-                if (bias && !bias_m && n0 + n < P.N) v[e] += bias[n0 + n];
+            for (int j = 0; j < 16; ++j) sum[q * 16 + j] += __uint_as_float(v[j]);
+          }
+          asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+        }
+        mbar_arrive(&dempty[acc]);
+        if (e == 0) mark(4, g);
+      }
+      gc += nchunks;
+      if (e == 0) mark(5, 1);
+      if (e == 0 && blockIdx.x == 0 && ok) g_gemm_tc_dbg[3] += 1;
+      float* C = partial ? P.ws + ((int64_t)U.sp * P.batch + U.zb) * P.M * P.N
+                         : P.C + (int64_t)U.i1 * P.c_batch + (int64_t)U.i2 * P.c_batch2;
+      if (P.tma_store) {
+        const float brow = (bias && bias_m && U.m0 + r < P.M) ? bias[U.m0 + r] : 0.f;
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          // the previous TMA store must be done reading the staging buffer
+          if (e == 0) asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+          asm volatile("bar.sync 2, 256;" ::: "memory");
+          if (ok) {
+            if (!colmaj) {
+              // half h = sub-tiles 2h, 2h+1 = the columns held by the hh == h warps
+              if (hh == h) {
+#pragma unroll
+                for (int jj = 0; jj < 2; ++jj) {
+#pragma unroll
+                  for (int c = 0; c < 8; ++c) {
+                    float v[4];
+#pragma unroll
+                    for (int q = 0; q < 4; ++q) {
+                      const int j = 32 * jj + 4 * c + q;
+                      v[q] = sum[j] * alpha + brow;
+                      if (bias && !bias_m && U.n0 + cb + j < P.N) v[q] += bias[U.n0 + cb + j];
+                    }
+                    *reinterpret_cast<float4*>(epi + jj * TC_TILE_BYTES + r * 128 + ((c ^ (r & 7)) << 4)) =
+                        make_float4(v[0], v[1], v[2], v[3]);
+                  }
+                }
               }
-              *reinterpret_cast<float4*>(smem + j * TC_TILE_BYTES + r * 128 + ((c ^ (r & 7)) << 4)) =
-                  make_float4(v[0], v[1], v[2], v[3]);
-            }
-          }
-        } else {
-          uint8_t* sub = smem + (r >> 5) * TC_TILE_BYTES + ((r & 3) << 2);
-          const int mc = (r & 31) >> 2;
+            } else if ((r >> 6) == h) {
+              // half h = sub-tiles of tile rows 64h..64h+63, every column line
+              uint8_t* sub = epi + ((r >> 5) & 1) * TC_TILE_BYTES + ((r & 3) << 2);
+              const int mc = (r & 31) >> 2;
 #pragma unroll
-          for (int n = 0; n < TC_BN; ++n) {
-            float v = sum[n] * alpha + brow;
-            if (bias && !bias_m && n0 + n < P.N) v += bias[n0 + n];
-            *reinterpret_cast<float*>(sub + n * 128 + ((mc ^ (n & 7)) << 4)) = v;
-          }
-        }
-      }
-      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-      asm volatile("bar.sync 1, 128;" ::: "memory");
-      if (t == 0 && ok) {
-        const int z2 = partial ? sp * (int)P.batch + (int)zb : i1;
-        const int z3 = partial ? 0 : i2;
-        const int64_t inner0 = colmaj ? m0 : n0, inner_n = colmaj ? P.M : P.N;
-        const int outer0 = (int)(colmaj ? n0 : m0);
-#pragma unroll
-        for (int j = 0; j < 4; ++j)
-          if (inner0 + 32 * j < inner_n)
-            tma_store_4d(&tmC, smem + j * TC_TILE_BYTES, (int)(inner0 + 32 * j), outer0, z2, z3);
-        asm volatile("cp.async.bulk.commit_group;" ::: "memory");
-        asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
-      }
-    } else if (cn == 1 || cm == 1) {
-      if (ok) {
-        if (!colmaj) {
-#pragma unroll
-          for (int q = 0; q < TC_BN / 4; ++q)
-            *reinterpret_cast<float4*>(T + r * LD + 4 * q) =
-                make_float4(sum[4 * q], sum[4 * q + 1], sum[4 * q + 2], sum[4 * q + 3]);
-        } else {
-#pragma unroll
-          for (int j = 0; j < TC_BN; ++j) T[j * LD + r] = sum[j];
-        }
-      }
-      if (t == 0) mark(5, 3);
-      asm volatile("bar.sync 1, 128;" ::: "memory");
-      if (t == 0) mark(5, 4);
-      // line = tile row (row-major C) or tile column (column-major C)
-      const int64_t rows_left = P.M - m0 < TC_BM ? P.M - m0 : TC_BM;
-      const int64_t cols_left = P.N - n0 < TC_BN ? P.N - n0 : TC_BN;
-      const int64_t nlines = colmaj ? cols_left : rows_left;
-      const int64_t nelem = colmaj ? rows_left : cols_left;
-      const int e0 = lane * 4;
-      const bool by_line = colmaj != bias_m;  // bias follows n: the line (column-major C) or the element
-      const int64_t bbase = bias_m ? m0 : n0;
-      // 8 lines in flight per warp: all shared loads, then all global stores
-#pragma unroll 1
-      for (int i0 = 0; ok && i0 < TC_BM / 4; i0 += 8) {
-        float4 x[8];
-#pragma unroll
-        for (int u = 0; u < 8; ++u) {
-          const int ln = g + 4 * (i0 + u);
-          x[u] = ln < nlines ? *reinterpret_cast<const float4*>(T + ln * LD + e0) : make_float4(0.f, 0.f, 0.f, 0.f);
-        }
-#pragma unroll
-        for (int u = 0; u < 8; ++u) {
-          const int ln = g + 4 * (i0 + u);
-          if (ln >= nlines) break;
-          float* lp = colmaj ? C + (n0 + ln) * cn + m0 : C + (m0 + ln) * cm + n0;
-          float v[4] = {x[u].x * alpha, x[u].y * alpha, x[u].z * alpha, x[u].w * alpha};
-          if (bias) {
-#pragma unroll
-            for (int e = 0; e < 4; ++e)
-              if (by_line || e0 + e < nelem) v[e] += bias[bbase + (by_line ? ln : e0 + e)];
-          }
-          if (e0 + 3 < nelem && ((reinterpret_cast<uintptr_t>(lp + e0) & 15) == 0)) {
-            float4* d4 = reinterpret_cast<float4*>(lp + e0);
-            if (accumulate) {
-              const float4 o = *d4;
-              v[0] += o.x; v[1] += o.y; v[2] += o.z; v[3] += o.w;
-            }
-            *d4 = make_float4(v[0], v[1], v[2], v[3]);
-          } else {
-#pragma unroll
-            for (int e = 0; e < 4; ++e) {
-              if (e0 + e < nelem) {
-                float* d = lp + e0 + e;
-                *d = accumulate ? *d + v[e] : v[e];
+              for (int j = 0; j < 64; ++j) {
+                const int n = cb + j;
+                float v = sum[j] * alpha + brow;
+                if (bias && !bias_m && U.n0 + n < P.N) v += bias[U.n0 + n];
+                *reinterpret_cast<float*>(sub + n * 128 + ((mc ^ (n & 7)) << 4)) = v;
               }
             }
           }
-        }
-      }
-    } else if (ok) {
-      // neither stride is 1: element by element from registers
-      const int64_t row = m0 + r;
-      if (row < P.M) {
+          asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+          asm volatile("bar.sync 2, 256;" ::: "memory");
+          if (e == 0 && ok) {
+            const int z2 = partial ? U.sp * (int)P.batch + (int)U.zb : U.i1;
+            const int z3 = partial ? 0 : U.i2;
+            const int64_t inner0 = colmaj ? U.m0 : U.n0, inner_n = colmaj ? P.M : P.N;
+            const int outer0 = (int)(colmaj ? U.n0 : U.m0);
 #pragma unroll
-        for (int j = 0; j < TC_BN; ++j) {
-          const int64_t col = n0 + j;
-          if (col < P.N) {
-            float v = sum[j] * alpha;
-            if (bias) v += bias[bias_m ? row : col];
-            float* d = C + row * cm + col * cn;
-            *d = accumulate ? *d + v : v;
+            for (int jj = 0; jj < 2; ++jj) {
+              const int64_t i0 = inner0 + 32 * (2 * h + jj);
+              if (i0 < inner_n) tma_store_4d(&tmC, epi + jj * TC_TILE_BYTES, (int)i0, outer0, z2, z3);
+            }
+            asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+          }
+        }
+      } else if (ok) {
+        // plain stores: accumulation into C, or a C layout TMA cannot describe
+        const int64_t row = U.m0 + r;
+        if (row < P.M) {
+#pragma unroll
+          for (int j = 0; j < 64; ++j) {
+            const int64_t col = U.n0 + cb + j;
+            if (col < P.N) {
+              float v = sum[j] * alpha;
+              if (bias) v += bias[bias_m ? row : col];
+              float* d = C + row * cm + col * cn;
+              *d = accumulate ? *d + v : v;
+            }
           }
         }
       }
+      if (e == 0) mark(5, 2);
     }
+    if (e == 0) asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
   }
-  if (threadIdx.x == 64) mark(5, 2);
   __syncthreads();
   if (warp == 1) {
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
@@ -714,7 +714,10 @@ bool launch_gemm_tc(const GemmDesc& g, cudaStream_t s) {
   // when C's layout is not TMA-describable or the result accumulates.
   CUtensorMap tc;
   memset(&tc, 0, sizeof tc);
-  if (splits > 1) {
+  static const bool tma_store_ok = [] { const char* e = getenv("TG_GEMM_TMA_STORE"); return !(e && e[0] == '0'); }();
+  if (!tma_store_ok) {
+    p.tma_store = 0;
+  } else if (splits > 1) {
     p.tma_store = make_map(&tc, g.workspace, true, M, N, N, 1, (int64_t)splits * g.batch, M * N, 1, 0) ? 1 : 0;
   } else if (!g.accumulate && (c_n == 1 || c_m == 1)) {
     const bool cmaj = c_m == 1 && c_n != 1;
@@ -729,8 +732,10 @@ bool launch_gemm_tc(const GemmDesc& g, cudaStream_t s) {
       return false;
     attr = true;
   }
-  dim3 grid((unsigned)((N + TC_BN - 1) / TC_BN), (unsigned)((M + TC_BM - 1) / TC_BM), (unsigned)(g.batch * splits));
-  gemm_tc_kernel<<<grid, 192, TC_SMEM, s>>>(ta, tb, tc, p);
+  p.units = ((N + TC_BN - 1) / TC_BN) * ((M + TC_BM - 1) / TC_BM) * g.batch * splits;
+  const int64_t sms = device_sm_count();
+  const unsigned grid = (unsigned)(p.units < sms ? p.units : sms);
+  gemm_tc_kernel<<<grid, 448, TC_SMEM, s>>>(ta, tb, tc, p);
   if (splits > 1) {
     int64_t total = g.batch * M * N;
     int64_t blocks = (total + 255) / 256, cap = (int64_t)device_sm_count() * 8;

@@ -300,7 +300,9 @@ void Graph::plan_storage() {
       }
       TG_CUDA(cudaMalloc(&arena_[a], (size_t)bump[a]));
       arena_owned_[a] = true;
-      TG_CUDA(cudaMemset(arena_[a], 0, (size_t)bump[a]));
+      // On the context's stream: it is non-blocking, so a clear on the legacy
+      // default stream would be unordered with the uploads and steps after it.
+      TG_CUDA(cudaMemsetAsync(arena_[a], 0, (size_t)bump[a], ctx->stream));
     }
   }
   if (parent) {

@@ -13,7 +13,7 @@ pytestmark = pytest.mark.gpu
 
 
 @pytest.mark.parametrize("ta,tb", [(False, False), (False, True), (True, False), (True, True)])
-@pytest.mark.parametrize("M,K,N", [(300, 200, 260), (128, 64, 128), (1000, 96, 70)])
+@pytest.mark.parametrize("M,K,N", [(300, 200, 260), (128, 64, 128), (1000, 96, 70), (256, 200, 30), (256, 30, 200)])
 def test_gemm_layouts(ctx, ta, tb, M, K, N):
     a = rnd([K, M] if ta else [M, K], 40)
     b = rnd([N, K] if tb else [K, N], 41)
