@@ -36,6 +36,7 @@ sys.path.insert(0, ROOT)
 from tensorgrad_b200 import configs as CF  # noqa: E402
 
 METRIC = "train samples/sec (GPT d384 L6 T256, config 4)"
+GEMM_DRAM_BYTES_PER_LAUNCH = 10696.4e6 / 132  # ncu capture, profiles/c4_step_launches.md
 UNIT = "samples/s"
 
 
@@ -247,9 +248,16 @@ def main():
     gemm_ms = sum(t for k, t in zip(kinds, prof) if k in ("matmul", "matmul_batched"))
     gemm_fl = sum(gemm_flops_of(ir.program, kinds))
     dom = max(by_kind.items(), key=lambda kv: kv[1])[0]
+    n_gemm = sum(1 for k in kinds if k in ("matmul", "matmul_batched"))
     roof = {"bound": "tensor", "kernel": "matmul+matmul_batched (all GEMM launches of one step)",
             "achieved": gemm_fl / (gemm_ms * 1e-3) / 1e12 if gemm_ms > 0 else None, "peak": bf16,
-            "unit": "TFLOP/s", "peak_source": f"{src} bf16 dense (MEASURED_PEAKS.json)", "traffic": None}
+            "unit": "TFLOP/s", "peak_source": f"{src} bf16 dense (MEASURED_PEAKS.json)",
+            # DRAM bytes of the GEMM launches of one step: the average per launch of one ncu
+            # capture (profiles/c4_step_launches.md: 10696 MB over 132 gemm_tc launches) times
+            # this step's GEMM launches; algorithmic operand+output bytes are far lower because
+            # operand tiles are re-read from L2, not DRAM
+            "traffic": GEMM_DRAM_BYTES_PER_LAUNCH * n_gemm if args.config == "c4" and not args.batch else None,
+            "traffic_unit": "bytes per step (GEMM class)"}
     roof["frac"] = roof["achieved"] / bf16 if roof["achieved"] else None
     roof["frac_of_3xtf32_effective"] = roof["achieved"] / (bf16 / 6.0) if roof["achieved"] else None
     roof["dominant_kind"] = dom

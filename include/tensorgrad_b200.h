@@ -95,8 +95,9 @@ int tg_read_tensor(tg_ctx* ctx, int graph_id, int tensor_id, void* out);
 int tg_launch_list(tg_ctx* ctx, int graph_id, char* buf, size_t cap, size_t* needed);
 
 /* Plans a program without a GPU and writes JSON {"info", "launches",
- * "kernelSources"}: the graph info, the label of every launch one step would
- * make, and the CUDA source of every fused elementwise kernel. No device
+ * "kernelSources", "kernelPreamble"}: the graph info, the label of every
+ * launch one step would make, the CUDA source of every fused elementwise
+ * kernel and the helper preamble they are compiled with. No device
  * memory is allocated and nothing is compiled or run. No counterpart in the
  * reference (its codegen.ts plan is only visible through the WGSL it emits);
  * used to test planner decisions on machines without a GPU. */

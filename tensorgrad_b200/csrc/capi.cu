@@ -140,7 +140,7 @@ int tg_plan_dry(const char* program_json, size_t len, int world, char* buf, size
     }
     s += "],\"kernelSources\":[";
     for (size_t i = 0; i < g.jit_sources().size(); ++i) s += (i ? "," : "") + q(g.jit_sources()[i]);
-    s += "]}";
+    s += "],\"kernelPreamble\":" + q(tg::jit_preamble()) + "}";
     write_str(s, buf, cap, needed);
   });
 }
