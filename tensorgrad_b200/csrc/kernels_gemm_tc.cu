@@ -57,14 +57,19 @@ __device__ int g_gemm_tc_dbg[8];
 constexpr int TC_TRACE_N = 64;
 __device__ long long g_gemm_tc_trace[6][TC_TRACE_N];
 
-constexpr int TC_BM = 128, TC_BN = 128, TC_BK = 32, TC_STAGES = 3;
+constexpr int TC_BM = 128, TC_BN = 128, TC_BK = 32;
 constexpr int TC_TILE_BYTES = 128 * TC_BK * 4;  // 16 KB per operand tile
 // Per stage: [0] A as landed by TMA, [1] B hi (K-major MMA operand; TMA lands
 // a K-major B here and it is split in place), [2] B lo, [3] B as landed when
-// it is MN-major.
-constexpr int TC_STAGE_BYTES = 4 * TC_TILE_BYTES;
+// it is MN-major. A K-major B needs no slot 3, so its ring has four 48 KB
+// stages instead of three 64 KB ones: the same 192 KB, and a deeper pipeline
+// to hide the TMA latency (1.5-2.5K cycles) plus the split (about 1K).
+constexpr int TC_RING_BYTES = 12 * TC_TILE_BYTES;
+template <int NS> struct TcRing {
+  static constexpr int stage_bytes = TC_RING_BYTES / NS;
+};
 constexpr int TC_EPI_BYTES = 2 * TC_TILE_BYTES;  // output staging: half a tile at a time
-constexpr int TC_SMEM = TC_STAGES * TC_STAGE_BYTES + TC_EPI_BYTES + 1024 + 256;
+constexpr int TC_SMEM = TC_RING_BYTES + TC_EPI_BYTES + 1024 + 256;
 constexpr uint32_t TC_TMEM_COLS = 512;
 constexpr uint32_t TC_ACOL = 2 * TC_BN;  // first TMEM column of the per-stage A hi/lo (64 columns each)
 constexpr long long TC_SPIN_LIMIT = 1ll << 22;
@@ -302,20 +307,22 @@ __device__ __forceinline__ void split_b(uint8_t* st, int t, bool kmajor) {
 // Persistent: each CTA walks units blockIdx.x, blockIdx.x + gridDim.x, ...;
 // the stage ring, the accumulator pair and every barrier phase continue
 // across units, so one unit's epilogue overlaps the next unit's main loop.
+template <int NS>
 __global__ void __launch_bounds__(448, 1) gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA,
                                                          const __grid_constant__ CUtensorMap tmB,
                                                          const __grid_constant__ CUtensorMap tmC,
                                                          const __grid_constant__ TcParams P) {
+  constexpr int SB = TcRing<NS>::stage_bytes;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   // 1 KB-aligned base for the 128B-swizzled tiles. Offsetting the shared
   // array (rather than casting through an integer) keeps the pointer in the
   // shared address space, so tile accesses compile to shared loads/stores.
   uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
-  uint8_t* epi = smem + TC_STAGES * TC_STAGE_BYTES;  // two output sub-tiles
+  uint8_t* epi = smem + TC_RING_BYTES;  // two output sub-tiles
   uint64_t* full = reinterpret_cast<uint64_t*>(epi + TC_EPI_BYTES);
-  uint64_t* conv = full + TC_STAGES;
-  uint64_t* empty = conv + TC_STAGES;
-  uint64_t* dfull = empty + TC_STAGES;   // [2] accumulator chunk finished (MMA commit)
+  uint64_t* conv = full + NS;
+  uint64_t* empty = conv + NS;
+  uint64_t* dfull = empty + NS;   // [2] accumulator chunk finished (MMA commit)
   uint64_t* dempty = dfull + 2;          // [2] accumulator drained (256 epilogue threads)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(dempty + 2);
 
@@ -327,7 +334,7 @@ __global__ void __launch_bounds__(448, 1) gemm_tc_kernel(const __grid_constant__
   };
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < TC_STAGES; ++s) {
+    for (int s = 0; s < NS; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&conv[s], 128);
       mbar_init(&empty[s], 1);
@@ -358,10 +365,10 @@ __global__ void __launch_bounds__(448, 1) gemm_tc_kernel(const __grid_constant__
         const int ab1 = P.a_b1 ? U.i1 : 0, ab2 = P.a_b2 ? U.i2 : 0;
         const int bb1 = P.b_b1 ? U.i1 : 0, bb2 = P.b_b2 ? U.i2 : 0;
         for (int it = 0; it < U.nk; ++it, ++gs) {
-          const int s = gs % TC_STAGES;
-          const uint32_t ph = (uint32_t)(gs / TC_STAGES) & 1u;
-          if (gs >= TC_STAGES && !mbar_wait(&empty[s], ph ^ 1u, 1)) { ok = false; break; }
-          uint8_t* st = smem + s * TC_STAGE_BYTES;
+          const int s = gs % NS;
+          const uint32_t ph = (uint32_t)(gs / NS) & 1u;
+          if (gs >= NS && !mbar_wait(&empty[s], ph ^ 1u, 1)) { ok = false; break; }
+          uint8_t* st = smem + s * SB;
           mark(0, gs);
           if (blockIdx.x == 0) g_gemm_tc_dbg[0] = gs + 1;
           mbar_expect_tx(&full[s], 2 * TC_TILE_BYTES);
@@ -385,8 +392,8 @@ __global__ void __launch_bounds__(448, 1) gemm_tc_kernel(const __grid_constant__
       for (int64_t u = blockIdx.x; u < P.units && ok; u += gridDim.x) {
         const TcUnit U = tc_unit(P, u);
         for (int it = 0; it < U.nk; ++it, ++gs) {
-          const int s = gs % TC_STAGES;
-          const uint32_t ph = (uint32_t)(gs / TC_STAGES) & 1u;
+          const int s = gs % NS;
+          const uint32_t ph = (uint32_t)(gs / NS) & 1u;
           const int c = gc + it / TC_CHUNK, acc = c & 1;
           const bool chunk_start = (it % TC_CHUNK) == 0;
           if (chunk_start && c >= 2 && !mbar_wait(&dempty[acc], (uint32_t)((c - 2) >> 1) & 1u, 5)) {
@@ -394,7 +401,7 @@ __global__ void __launch_bounds__(448, 1) gemm_tc_kernel(const __grid_constant__
           }
           if (!mbar_wait(&conv[s], ph, 2)) { ok = false; break; }
           asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-          const uint32_t base = smem_u32(smem + s * TC_STAGE_BYTES);
+          const uint32_t base = smem_u32(smem + s * SB);
           const uint32_t b_hi = base + TC_TILE_BYTES, b_lo = base + 2 * TC_TILE_BYTES;
           const uint32_t a_hi = tmem + TC_ACOL + 64u * (uint32_t)s, a_lo = a_hi + 32u;
           const uint32_t dacc = tmem + (uint32_t)(acc * TC_BN);
@@ -425,11 +432,11 @@ __global__ void __launch_bounds__(448, 1) gemm_tc_kernel(const __grid_constant__
     for (int64_t u = blockIdx.x; u < P.units && ok; u += gridDim.x) {
       const TcUnit U = tc_unit(P, u);
       for (int it = 0; it < U.nk; ++it, ++gs) {
-        const int s = gs % TC_STAGES;
-        const uint32_t ph = (uint32_t)(gs / TC_STAGES) & 1u;
+        const int s = gs % NS;
+        const uint32_t ph = (uint32_t)(gs / NS) & 1u;
         if (!mbar_wait(&full[s], ph, 3)) { ok = false; break; }
         if (t == 0) mark(1, gs);
-        uint8_t* st = smem + s * TC_STAGE_BYTES;
+        uint8_t* st = smem + s * SB;
         split_a_row(st, r, P.a_kmajor != 0, tmem + lane_base + TC_ACOL + 64u * (uint32_t)s);
         split_b(st, t, P.b_kmajor != 0);
         asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
@@ -728,14 +735,16 @@ bool launch_gemm_tc(const GemmDesc& g, cudaStream_t s) {
 
   static bool attr = false;
   if (!attr) {
-    if (cudaFuncSetAttribute(gemm_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, TC_SMEM) != cudaSuccess)
+    if (cudaFuncSetAttribute(gemm_tc_kernel<3>, cudaFuncAttributeMaxDynamicSharedMemorySize, TC_SMEM) != cudaSuccess ||
+        cudaFuncSetAttribute(gemm_tc_kernel<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, TC_SMEM) != cudaSuccess)
       return false;
     attr = true;
   }
   p.units = ((N + TC_BN - 1) / TC_BN) * ((M + TC_BM - 1) / TC_BM) * g.batch * splits;
   const int64_t sms = device_sm_count();
   const unsigned grid = (unsigned)(p.units < sms ? p.units : sms);
-  gemm_tc_kernel<<<grid, 448, TC_SMEM, s>>>(ta, tb, tc, p);
+  if (bk) gemm_tc_kernel<4><<<grid, 448, TC_SMEM, s>>>(ta, tb, tc, p);
+  else gemm_tc_kernel<3><<<grid, 448, TC_SMEM, s>>>(ta, tb, tc, p);
   if (splits > 1) {
     int64_t total = g.batch * M * N;
     int64_t blocks = (total + 255) / 256, cap = (int64_t)device_sm_count() * 8;

@@ -229,9 +229,78 @@ size_t row_scratch_floats(int kind, int64_t rows, int64_t D) {
   return c > 1 ? (size_t)(rows * c) : 0;
 }
 
+// Softmax / logSoftmax of rows up to 32*NV long with the row held in
+// registers: one load, a warp max, one exp per element, a warp sum, one
+// store (element j of the row lives in lane j % 32, slot j / 32, so every
+// load and store is a coalesced 128-byte warp access).
+template <int KIND, int NV>
+__global__ void __launch_bounds__(256) row_softmax_reg_kernel(const float* __restrict__ x, float* __restrict__ out,
+                                                              int64_t rows, int64_t D) {
+  const int lane = threadIdx.x & 31;
+  const int64_t warp = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
+  for (int64_t r = warp; r < rows; r += nwarps) {
+    const float* xr = x + r * D;
+    const int64_t lim = (KIND == ROW_SOFTMAX_CAUSAL) ? (r % D) + 1 : D;
+    float v[NV];
+    float m = -INFINITY;
+#pragma unroll
+    for (int i = 0; i < NV; ++i) {
+      const int64_t j = lane + 32 * i;
+      v[i] = j < lim ? __ldg(xr + j) : -INFINITY;
+      m = fmaxf(m, v[i]);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    float sum = 0.f;
+#pragma unroll
+    for (int i = 0; i < NV; ++i) {
+      const int64_t j = lane + 32 * i;
+      const float e = j < lim ? expf(v[i] - m) : 0.f;
+      if (KIND == ROW_SOFTMAX_CAUSAL) v[i] = e;
+      sum += e;
+    }
+    sum = warp_sum(sum);
+    float* o = out + r * D;
+    if (KIND == ROW_LOGSOFTMAX) {
+      const float lz = m + logf(sum);
+#pragma unroll
+      for (int i = 0; i < NV; ++i) {
+        const int64_t j = lane + 32 * i;
+        if (j < D) o[j] = v[i] - lz;
+      }
+    } else {
+#pragma unroll
+      for (int i = 0; i < NV; ++i) {
+        const int64_t j = lane + 32 * i;
+        if (j < D) o[j] = j < lim ? __fdiv_rn(v[i], sum) : 0.f;
+      }
+    }
+  }
+}
+
+template <int KIND>
+static bool launch_softmax_reg(const float* x, float* out, int64_t rows, int64_t D, cudaStream_t s) {
+  int64_t warps_per_block = 8, blocks = (rows + warps_per_block - 1) / warps_per_block;
+  const int64_t cap = (int64_t)device_sm_count() * 16;
+  const unsigned g = (unsigned)(blocks < cap ? blocks : cap);
+  if (D <= 32) row_softmax_reg_kernel<KIND, 1><<<g, 256, 0, s>>>(x, out, rows, D);
+  else if (D <= 64) row_softmax_reg_kernel<KIND, 2><<<g, 256, 0, s>>>(x, out, rows, D);
+  else if (D <= 128) row_softmax_reg_kernel<KIND, 4><<<g, 256, 0, s>>>(x, out, rows, D);
+  else if (D <= 256) row_softmax_reg_kernel<KIND, 8><<<g, 256, 0, s>>>(x, out, rows, D);
+  else if (D <= 512) row_softmax_reg_kernel<KIND, 16><<<g, 256, 0, s>>>(x, out, rows, D);
+  else if (D <= 1024) row_softmax_reg_kernel<KIND, 32><<<g, 256, 0, s>>>(x, out, rows, D);
+  else return false;
+  return true;
+}
+
 void launch_row(int kind, const float* x, void* out, int64_t rows, int64_t D, cudaStream_t s, const int* seed,
                 uint32_t salt, float* scratch, size_t scratch_floats) {
   if (rows <= 0) return;
+  if (kind == ROW_SOFTMAX_CAUSAL && launch_softmax_reg<ROW_SOFTMAX_CAUSAL>(x, reinterpret_cast<float*>(out), rows, D, s))
+    return;
+  if (kind == ROW_LOGSOFTMAX && launch_softmax_reg<ROW_LOGSOFTMAX>(x, reinterpret_cast<float*>(out), rows, D, s))
+    return;
   if (kind == ROW_SUM || kind == ROW_MEAN) {
     int64_t c = long_row_chunks(rows, D);
     if (c > 1 && scratch && scratch_floats >= (size_t)(rows * c)) {
@@ -276,18 +345,46 @@ __global__ void __launch_bounds__(256) colsum_partial_kernel(const float* __rest
   int64_t c = blockIdx.y;
   if (col >= inner) return;
   int64_t r0 = c * rows_per, r1 = r0 + rows_per < outer ? r0 + rows_per : outer;
+  // rows in ascending order; 8 independent loads in flight per thread
   float s = 0.f;
-  for (int64_t r = r0; r < r1; ++r) s += x[r * inner + col];
+  int64_t r = r0;
+  for (; r + 8 <= r1; r += 8) {
+    float v[8];
+#pragma unroll
+    for (int u = 0; u < 8; ++u) v[u] = __ldg(x + (r + u) * inner + col);
+#pragma unroll
+    for (int u = 0; u < 8; ++u) s += v[u];
+  }
+  for (; r < r1; ++r) s += __ldg(x + r * inner + col);
   part[c * inner + col] = s;
 }
 
+// 32 columns per block; warp w sums chunks w, w+8, ... (coalesced across the
+// warp's 32 columns), then the 8 warp sums are added in warp order. The
+// order is fixed, so results are deterministic.
 __global__ void __launch_bounds__(256) colsum_fold_kernel(const float* __restrict__ part, float* __restrict__ out,
                                                           int64_t nchunk, int64_t inner) {
-  int64_t col = (int64_t)blockIdx.x * 256 + threadIdx.x;
-  if (col >= inner) return;
+  __shared__ float red[8][33];
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+  const int64_t col = (int64_t)blockIdx.x * 32 + lane;
   float s = 0.f;
-  for (int64_t c = 0; c < nchunk; ++c) s += part[c * inner + col];
-  out[col] = s;
+  if (col < inner) {
+    int64_t c = w;
+    for (; c + 24 < nchunk; c += 32) {
+      const float a = __ldg(part + c * inner + col), b = __ldg(part + (c + 8) * inner + col);
+      const float d = __ldg(part + (c + 16) * inner + col), e = __ldg(part + (c + 24) * inner + col);
+      s += a; s += b; s += d; s += e;
+    }
+    for (; c < nchunk; c += 8) s += __ldg(part + c * inner + col);
+  }
+  red[w][lane] = s;
+  __syncthreads();
+  if (w == 0 && col < inner) {
+    float t = 0.f;
+#pragma unroll
+    for (int k = 0; k < 8; ++k) t += red[k][lane];
+    out[col] = t;
+  }
 }
 
 void launch_colsum(const float* x, float* out, int64_t outer, int64_t inner, float* scratch, cudaStream_t s) {
@@ -300,7 +397,7 @@ void launch_colsum(const float* x, float* out, int64_t outer, int64_t inner, flo
   }
   int64_t rows_per = (outer + c - 1) / c;
   colsum_partial_kernel<<<dim3(gx, (unsigned)c), 256, 0, s>>>(x, scratch, outer, inner, rows_per);
-  colsum_fold_kernel<<<gx, 256, 0, s>>>(scratch, out, c, inner);
+  colsum_fold_kernel<<<(unsigned)((inner + 31) / 32), 256, 0, s>>>(scratch, out, c, inner);
 }
 
 // ---------------------------------------------------- general sum to shape --
