@@ -135,9 +135,9 @@ void jit_compile_pending() {
   g_pending.clear();
 }
 
-void jit_launch(const JitFn& f, unsigned grid, unsigned block, void** args, cudaStream_t s) {
+void jit_launch(const JitFn& f, unsigned grid_x, unsigned grid_y, unsigned block, void** args, cudaStream_t s) {
   if (!f.fn) throw TgError("Error", "internal: kernel " + f.name + " was not compiled");
-  CUresult r = drv().launch(reinterpret_cast<CUfunction>(f.fn), grid, 1, 1, block, 1, 1, 0,
+  CUresult r = drv().launch(reinterpret_cast<CUfunction>(f.fn), grid_x, grid_y, 1, block, 1, 1, 0,
                             reinterpret_cast<CUstream>(s), args, nullptr);
   if (r != CUDA_SUCCESS) throw TgError("CudaError", "launch " + f.name + ": " + cu_err(r));
 }

@@ -96,6 +96,10 @@ size_t row_scratch_floats(int kind, int64_t rows, int64_t D);
 
 // Column sums [outer, inner] -> [inner] (deterministic two-pass with scratch).
 size_t colsum_scratch_floats(int64_t outer, int64_t inner);
+// Chunking of the two-pass column sum (chunks of consecutive rows) and its
+// second pass, shared with generated kernels that compute the first pass.
+int64_t colsum_chunks(int64_t outer, int64_t inner);
+void launch_colsum_fold(const float* part, float* out, int64_t nchunk, int64_t inner, cudaStream_t s);
 void launch_colsum(const float* x, float* out, int64_t outer, int64_t inner, float* scratch, cudaStream_t s);
 // General sum-to-shape: keep[d] = 1 where the output keeps input axis d.
 void launch_sum_general(const float* x, float* out, int rank, const int64_t* in_dims, const int64_t* keep,

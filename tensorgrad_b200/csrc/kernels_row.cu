@@ -325,7 +325,7 @@ void launch_row(int kind, const float* x, void* out, int64_t rows, int64_t D, cu
 }
 
 // -------------------------------------------------------------- column sum --
-static int64_t colsum_chunks(int64_t outer, int64_t inner) {
+int64_t colsum_chunks(int64_t outer, int64_t inner) {
   int sms = device_sm_count();
   int64_t colblocks = (inner + 255) / 256;
   int64_t want = ((int64_t)sms * 4 + colblocks - 1) / colblocks;
@@ -385,6 +385,10 @@ __global__ void __launch_bounds__(256) colsum_fold_kernel(const float* __restric
     for (int k = 0; k < 8; ++k) t += red[k][lane];
     out[col] = t;
   }
+}
+
+void launch_colsum_fold(const float* part, float* out, int64_t nchunk, int64_t inner, cudaStream_t s) {
+  colsum_fold_kernel<<<(unsigned)((inner + 31) / 32), 256, 0, s>>>(part, out, nchunk, inner);
 }
 
 void launch_colsum(const float* x, float* out, int64_t outer, int64_t inner, float* scratch, cudaStream_t s) {

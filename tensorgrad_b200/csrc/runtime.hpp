@@ -64,7 +64,7 @@ struct JitFn {
 };
 std::shared_ptr<JitFn> jit_request(const std::string& name, const std::string& src);
 void jit_compile_pending();
-void jit_launch(const JitFn& f, unsigned grid, unsigned block, void** args, cudaStream_t s);
+void jit_launch(const JitFn& f, unsigned grid_x, unsigned grid_y, unsigned block, void** args, cudaStream_t s);
 const std::string& jit_preamble();
 
 struct Program {
@@ -158,10 +158,11 @@ class Graph {
   void plan_fusion();
   void emit_launches();
   EwInput ew_input(int t, const std::vector<int64_t>& oshape, bool& vec_ok);
-  void emit_ew_group(int root, const int* seed_ptr,
+  void emit_ew_group(int group, const int* seed_ptr, float* scratch, size_t scratch_floats,
                      const std::function<void(const std::string&, std::function<void(cudaStream_t)>)>& add);
-  int ew_pos(int i) const { return ew_root_.empty() || ew_root_[i] < 0 ? i : ew_root_[i]; }
   bool ew_internal(int t) const;
+  bool ew_is_absorbed(int i) const { return !ew_absorbed_.empty() && ew_absorbed_[i]; }
+  int ew_group_of(int i) const { return ew_group_.empty() ? -1 : ew_group_[i]; }
   void run_launches(cudaStream_t s);
   void init_constants();
   void* ptr(int t) const;
@@ -173,7 +174,16 @@ class Graph {
   std::vector<int> action_;          // per op: planned action code
   std::vector<StorageLoc> loc_;      // per root tensor
   std::vector<int> op_done_;         // ops folded away
-  std::vector<int> ew_root_;         // per op: root op of its fused elementwise group, or -1
+  // Fused elementwise groups. A group is rooted at the op whose output it
+  // writes: its last elementwise member, or a reduction that consumes it.
+  struct EwGroup {
+    std::vector<int> members;  // elementwise ops evaluated per element, ascending
+    int root = -1;             // op whose output the launch writes
+    int red = -1;              // the root when it is a reduction (sum_last, mean_last, sum_to_shape)
+  };
+  std::vector<EwGroup> ew_groups_;
+  std::vector<int> ew_group_;        // per op: group index when the op roots a group, else -1
+  std::vector<char> ew_absorbed_;    // per op: value computed inside the groups that use it (no storage)
   bool jit_ = false;                 // fused elementwise groups compiled at plan time
   std::vector<std::string> jit_sources_;  // generated kernel sources (planning-only contexts)
   void* arena_[AR_COUNT] = {};

@@ -161,13 +161,13 @@ void Graph::plan_storage() {
   };
   for (int i = 0; i < nO; ++i) {
     if (op_done_[i]) continue;
+    // An absorbed elementwise op has no output; the groups that evaluate it
+    // read its operands at their own positions.
+    if (ew_is_absorbed(i)) continue;
     int o = P.out[i];
-    // A fused elementwise group runs at its root op: its members' operands are
-    // read there, and values passed inside the group need no storage.
-    const int pos = ew_pos(i);
     // The op writes its output's root: its own storage, or (for a GEMM or
     // permute writing straight into a later permute's layout) that root.
-    if (!views_[o].onehot && !ew_internal(o)) {
+    if (!views_[o].onehot) {
       const int r = views_[o].root;
       used[r] = 1;
       if (def[r] < 0 || i < def[r]) def[r] = i;
@@ -181,8 +181,13 @@ void Graph::plan_storage() {
       touch(P.op(i)["b"].i32(), i);
       continue;
     }
+    const int g = ew_group_of(i);
+    if (g >= 0)
+      for (int m : ew_groups_[g].members)
+        for (int t : P.op_inputs[m])
+          if (!ew_internal(t)) touch(t, i);
     for (int t : P.op_inputs[i])
-      if (!ew_internal(t)) touch(t, pos);
+      if (!ew_internal(t)) touch(t, i);
   }
   for (int t : pinned) used[t] = 1;
   if (P.loss >= 0) { pinned.insert(views_[P.loss].root); used[views_[P.loss].root] = 1; }
@@ -504,6 +509,11 @@ void Graph::emit_launches() {
     }
     if (i == nO) break;
     if (op_done_[i]) continue;
+    if (ew_is_absorbed(i)) continue;
+    if (ew_group_of(i) >= 0) {
+      emit_ew_group(ew_group_of(i), seed_ptr, scratch, scratch_floats, add);
+      continue;
+    }
     const std::string& k = P.kind[i];
     const auto& O = P.op(i);
     int o = P.out[i];
@@ -533,10 +543,6 @@ void Graph::emit_launches() {
       continue;
     }
     // ---------------------------------------------------- elementwise --
-    if (jit_ && ew_root_[i] >= 0) {
-      if (ew_root_[i] == i) emit_ew_group(i, seed_ptr, add);
-      continue;
-    }
     static const std::map<std::string, int> bin = {{"add", EW_ADD}, {"sub", EW_SUB}, {"mul", EW_MUL},
                                                    {"div", EW_DIV}, {"min", EW_MIN}, {"max", EW_MAX}};
     static const std::map<std::string, int> un = {

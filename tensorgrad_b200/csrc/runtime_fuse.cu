@@ -21,6 +21,7 @@
 // Every op's arithmetic is the same f32 operation, rounded the same way, as
 // the unfused interpreter kernel (kernels_ew.cu) performs for it, so fusion
 // changes which values reach HBM, not the values.
+#include <algorithm>
 #include <cstring>
 #include <functional>
 #include <set>
@@ -89,14 +90,50 @@ constexpr int kMaxGroupOps = 48;
 }  // namespace
 
 bool Graph::ew_internal(int t) const {
-  if (ew_root_.empty()) return false;
-  int p = P.producer[t];
-  return p >= 0 && ew_root_[p] >= 0 && ew_root_[p] != p;
+  if (ew_absorbed_.empty()) return false;
+  const int p = P.producer[t];
+  return p >= 0 && ew_absorbed_[p];
 }
+
+namespace {
+// How a reduction consumes its input: along the last axis (rows) or the
+// leading axes (columns), or neither (not fused).
+enum RedShape { RED_NONE = 0, RED_ROW, RED_COL };
+RedShape red_shape(const Program& P, int r, int64_t* rows, int64_t* len) {
+  const std::string& k = P.kind[r];
+  if (k != "sum_last" && k != "mean_last" && k != "sum_to_shape") return RED_NONE;
+  const int a = P.op(r)["a"].i32();
+  const auto& is = P.T[a].shape;
+  const int64_t n = P.T[a].numel, on = P.T[P.out[r]].numel;
+  if (n <= 0 || on <= 0) return RED_NONE;
+  if (k == "sum_last" || k == "mean_last") {
+    *len = is.empty() ? 1 : is.back();
+    *rows = n / std::max<int64_t>(*len, 1);
+    return *len <= 4096 ? RED_ROW : RED_NONE;
+  }
+  if (k != "sum_to_shape") return RED_NONE;
+  const auto& os = P.T[P.out[r]].shape;
+  const int R = (int)is.size(), rd = R - (int)os.size();
+  std::vector<int> keep(R, 0);
+  for (int d = 0; d < R; ++d) keep[d] = (d >= rd && !(os[d - rd] == 1 && is[d] != 1)) ? 1 : 0;
+  bool prefix = true, suffix = true, seen_red = false, seen_keep = false;
+  for (int d = 0; d < R; ++d) {
+    if (is[d] == 1) continue;
+    if (!keep[d]) { seen_red = true; if (seen_keep) suffix = false; }
+    else { seen_keep = true; if (seen_red) prefix = false; }
+  }
+  if (on == n) return RED_NONE;  // nothing reduced (a view or a copy)
+  if (prefix && !suffix) { *rows = on; *len = n / on; return *len <= 4096 ? RED_ROW : RED_NONE; }
+  if (suffix && !prefix) { *rows = n / on; *len = on; return RED_COL; }
+  return RED_NONE;
+}
+}  // namespace
 
 void Graph::plan_fusion() {
   const int nO = (int)P.ops.size();
-  ew_root_.assign(nO, -1);
+  ew_group_.assign(nO, -1);
+  ew_absorbed_.assign(nO, 0);
+  ew_groups_.clear();
   jit_ = jit_enabled();
   if (!jit_) return;
   std::set<int> observable;
@@ -105,47 +142,105 @@ void Graph::plan_fusion() {
   for (auto& w : P.writebacks) observable.insert(w.src);
   for (auto& g : P.grads) observable.insert(g.second);
   if (P.loss >= 0) observable.insert(P.loss);
-  for (int i = 0; i < nO; ++i)
-    if (!op_done_[i] && action_[i] == 0 && ew_kinds().count(P.kind[i])) ew_root_[i] = i;
-
-  std::vector<std::vector<int>> members(nO);
-  std::vector<std::set<int>> ext(nO);  // tensors a group reads from memory
-  std::vector<char> posdep(nO, 0);     // group uses the element index (dropout, causal mask)
-  for (int i = 0; i < nO; ++i) posdep[i] = P.kind[i] == "dropout" || P.kind[i] == "where_causal";
+  auto is_ew = [&](int i) { return !op_done_[i] && action_[i] == 0 && ew_kinds().count(P.kind[i]) > 0; };
   auto side = [&](int i) { return P.opt_start >= 0 && i >= P.opt_start; };
+  // A produced tensor a consumer may evaluate in place: its own storage, not
+  // observable, and read at the consumer's shape or broadcast to it.
+  auto inlinable = [&](int t) {
+    const TView& v = views_[t];
+    return !observable.count(t) && v.root == t && !v.onehot && v.contiguous;
+  };
+
+  // Working state per op that roots a group.
+  std::vector<char> root(nO, 0), posdep(nO, 0);
+  std::vector<std::vector<int>> mem(nO);
+  std::vector<std::set<int>> ext(nO);  // tensors the group reads from memory
+  std::vector<int> copied(P.T.size(), 0);  // consumers that evaluate the tensor in place
+  auto full_inputs = [&](int p) {
+    int n = 0;
+    for (int t : ext[p]) if (P.T[t].numel >= P.T[P.out[p]].numel) ++n;
+    return n;
+  };
+  auto merge_into = [&](int i, int p, int t) -> bool {
+    std::set<int> merged = ext[i];
+    merged.erase(t);
+    merged.insert(ext[p].begin(), ext[p].end());
+    std::vector<int> m = mem[i];
+    m.insert(m.end(), mem[p].begin(), mem[p].end());
+    std::sort(m.begin(), m.end());
+    m.erase(std::unique(m.begin(), m.end()), m.end());
+    if ((int)merged.size() > kMaxGroupInputs || (int)m.size() > kMaxGroupOps) return false;
+    ext[i] = std::move(merged);
+    mem[i] = std::move(m);
+    posdep[i] = posdep[i] || posdep[p];
+    return true;
+  };
+
   for (int i = 0; i < nO; ++i) {
-    if (ew_root_[i] != i) continue;
-    members[i] = {i};
+    if (!is_ew(i)) continue;
+    root[i] = 1;
+    mem[i] = {i};
+    posdep[i] = P.kind[i] == "dropout" || P.kind[i] == "where_causal";
     for (int t : ew_operands(P, i)) ext[i].insert(t);
-    std::vector<int> ops_in = ew_operands(P, i);
     std::set<int> seen;
-    for (int t : ops_in) {
+    for (int t : ew_operands(P, i)) {
       if (!seen.insert(t).second) continue;
-      int p = P.producer[t];
-      if (p < 0 || ew_root_[p] != p || members[p].empty()) continue;
-      if (P.consumers[t].size() != 1 || P.consumers[t][0] != i) continue;
-      if (observable.count(t)) continue;
-      const TView& v = views_[t];
-      if (v.root != t || v.onehot || !v.contiguous) continue;
-      if (P.T[t].shape != P.T[P.out[i]].shape) {
-        // a smaller producer whose value the consumer reads broadcast is
-        // recomputed per output element; exact for pure elementwise ops, but
-        // not for ones that use the element's position
-        if (!broadcasts_to(P.T[t].shape, P.T[P.out[i]].shape) || posdep[p]) continue;
+      const int p = P.producer[t];
+      if (p < 0 || !root[p] || !inlinable(t) || side(p) != side(i)) continue;
+      if (P.T[t].shape != P.T[P.out[i]].shape &&
+          (!broadcasts_to(P.T[t].shape, P.T[P.out[i]].shape) || posdep[p]))
+        continue;
+      const auto& cs = P.consumers[t];
+      if (cs.size() == 1) {
+        // sole consumer: the producer's group moves into this one
+        if (merge_into(i, p, t)) { root[p] = 0; ext[p].clear(); }
+        continue;
       }
-      if (side(p) != side(i)) continue;
-      std::set<int> merged = ext[i];
-      merged.erase(t);
-      merged.insert(ext[p].begin(), ext[p].end());
-      if ((int)merged.size() > kMaxGroupInputs) continue;
-      if ((int)(members[i].size() + members[p].size()) > kMaxGroupOps) continue;
-      posdep[i] = posdep[i] || posdep[p];
-      for (int m : members[p]) ew_root_[m] = i;
-      members[i].insert(members[i].end(), members[p].begin(), members[p].end());
-      members[p].clear();
-      ext[p].clear();
-      ext[i] = std::move(merged);
+      // Several elementwise consumers of a cheap group (at most one input as
+      // large as its output, few ops): each consumer recomputes it rather than
+      // reading it back; once all of them do, it is never stored.
+      bool all_ew = true;
+      for (int c : cs)
+        if (!is_ew(c) || side(c) != side(p) ||
+            !broadcasts_to(P.T[t].shape, P.T[P.out[c]].shape) ||
+            (posdep[p] && P.T[t].shape != P.T[P.out[c]].shape))
+          all_ew = false;
+      if (!all_ew || full_inputs(p) > 1 || mem[p].size() > 16) continue;
+      if (merge_into(i, p, t)) ++copied[t];
     }
+  }
+  // Producers whose every consumer evaluates them in place are not stored.
+  for (int p = 0; p < nO; ++p)
+    if (root[p] && copied[P.out[p]] > 0 && copied[P.out[p]] == (int)P.consumers[P.out[p]].size()) root[p] = 0;
+
+  // A reduction over the output of a group it alone consumes evaluates the
+  // group per element instead of reading it back.
+  std::vector<int> red_of(nO, -1);
+  for (int r = 0; r < nO; ++r) {
+    if (op_done_[r] || action_[r] != 0) continue;
+    int64_t rows = 0, len = 0;
+    if (red_shape(P, r, &rows, &len) == RED_NONE) continue;
+    const int t = P.op(r)["a"].i32(), p = P.producer[t];
+    if (p < 0 || !root[p] || !inlinable(t) || side(p) != side(r)) continue;
+    if (P.consumers[t].size() != 1 || (int)ext[p].size() > kMaxGroupInputs) continue;
+    red_of[p] = r;
+  }
+
+  // Materialise the groups; every member not rooting one is absorbed.
+  for (int i = 0; i < nO; ++i)
+    if (is_ew(i) && !root[i]) ew_absorbed_[i] = 1;
+  for (int p = 0; p < nO; ++p) {
+    if (!root[p]) continue;
+    EwGroup g;
+    g.members = mem[p];
+    if (red_of[p] >= 0) {
+      ew_absorbed_[p] = 1;
+      g.root = g.red = red_of[p];
+    } else {
+      g.root = p;
+    }
+    ew_group_[g.root] = (int)ew_groups_.size();
+    ew_groups_.push_back(std::move(g));
   }
 }
 
@@ -217,31 +312,33 @@ std::string ew_expr(const Program& P, int i, const std::vector<std::string>& a, 
 
 }  // namespace
 
-void Graph::emit_ew_group(int r, const int* seed_ptr,
+void Graph::emit_ew_group(int gi, const int* seed_ptr, float* scratch, size_t scratch_floats,
                           const std::function<void(const std::string&, std::function<void(cudaStream_t)>)>& add) {
-  std::vector<int> mem;
-  for (int m = 0; m <= r; ++m)
-    if (ew_root_[m] == r) mem.push_back(m);
-  const int o = P.out[r];
-  const auto& os = P.T[o].shape;
-  const int64_t n = P.T[o].numel;
+  const EwGroup& G = ew_groups_[gi];
+  const std::set<int> member_set(G.members.begin(), G.members.end());
+  // The elementwise value the group produces: the root's output, or the
+  // reduction's input. Every member is evaluated at that value's shape.
+  const int vt = G.red >= 0 ? P.op(G.red)["a"].i32() : P.out[G.root];
+  const auto& os = P.T[vt].shape;
+  const int64_t n = P.T[vt].numel;
   if (n <= 0) return;
-  bool vec = true;
+  int64_t rows = 0, len = 0;
+  const RedShape rs = G.red >= 0 ? red_shape(P, G.red, &rows, &len) : RED_NONE;
+  if (G.red >= 0 && rs == RED_NONE) throw TgError("Error", "internal: fused reduction of an unsupported shape");
+  bool vec = rs == RED_NONE;
   std::vector<EwInput> ins;
-  std::vector<int> in_t;
   std::map<int, int> slot_of;
   bool has_drop = false;
   std::ostringstream ops;
   std::string label;
-  for (int m : mem) {
+  for (int m : G.members) {
     std::vector<std::string> a;
     for (int t : ew_operands(P, m)) {
-      if (ew_internal(t) && ew_root_[P.producer[t]] == r) { a.push_back("v" + std::to_string(t)); continue; }
+      if (member_set.count(P.producer[t])) { a.push_back("v" + std::to_string(t)); continue; }
       auto it = slot_of.find(t);
       if (it == slot_of.end()) {
         it = slot_of.emplace(t, (int)ins.size()).first;
         ins.push_back(ew_input(t, os, vec));
-        in_t.push_back(t);
       }
       a.push_back("x" + std::to_string(it->second));
     }
@@ -254,35 +351,35 @@ void Graph::emit_ew_group(int r, const int* seed_ptr,
     if (!label.empty()) label += "+";
     label += P.kind[m];
   }
-  void* out = ptr(o);
-  vec = vec && n % 4 == 0 && ((uintptr_t)out & 15) == 0;
+  const std::string value = "v" + std::to_string(vt);
+  void* out = ptr(P.out[G.root]);
+  if (rs == RED_NONE) vec = vec && n % 4 == 0 && ((uintptr_t)out & 15) == 0;
   const int R = (int)os.size();
 
-  // Per-lane values of each input (and, for the vector form, the loads that
-  // precede the lane loop).
+  // Per-element values of each input: for the vector form, loads before the
+  // 4-lane loop plus per-lane picks; otherwise one load per element index e.
   std::ostringstream pre, lane;
-  for (size_t s = 0; s < ins.size(); ++s) {
-    const EwInput& in = ins[s];
-    std::string p = "p" + std::to_string(s), x = "x" + std::to_string(s);
+  for (size_t si = 0; si < ins.size(); ++si) {
+    const EwInput& in = ins[si];
+    std::string p = "p" + std::to_string(si), x = "x" + std::to_string(si);
     std::string per = std::to_string(in.period) + "ll";
     switch (in.mode) {
       case IN_FULL:
-        if (vec) { pre << "    const float4 q" << s << " = __ldg(reinterpret_cast<const float4*>(" << p << " + i));\n";
-                   lane << "      const float " << x << " = f4(q" << s << ", l);\n"; }
+        if (vec) { pre << "    const float4 q" << si << " = __ldg(reinterpret_cast<const float4*>(" << p << " + i));\n";
+                   lane << "      const float " << x << " = f4(q" << si << ", l);\n"; }
         else lane << "      const float " << x << " = __ldg(" << p << " + e);\n";
         break;
       case IN_SCALAR:
-        pre << "    const float s" << s << " = __ldg(" << p << ");\n";
-        lane << "      const float " << x << " = s" << s << ";\n";
+        lane << "      const float " << x << " = __ldg(" << p << ");\n";
         break;
       case IN_PERIOD:
-        if (vec) { pre << "    const float4 q" << s << " = __ldg(reinterpret_cast<const float4*>(" << p << " + i % " << per << "));\n";
-                   lane << "      const float " << x << " = f4(q" << s << ", l);\n"; }
+        if (vec) { pre << "    const float4 q" << si << " = __ldg(reinterpret_cast<const float4*>(" << p << " + i % " << per << "));\n";
+                   lane << "      const float " << x << " = f4(q" << si << ", l);\n"; }
         else lane << "      const float " << x << " = __ldg(" << p << " + e % " << per << ");\n";
         break;
       case IN_ROWDIV:
-        if (vec) { pre << "    const float s" << s << " = __ldg(" << p << " + i / " << per << ");\n";
-                   lane << "      const float " << x << " = s" << s << ";\n"; }
+        if (vec) { pre << "    const float s" << si << " = __ldg(" << p << " + i / " << per << ");\n";
+                   lane << "      const float " << x << " = s" << si << ";\n"; }
         else lane << "      const float " << x << " = __ldg(" << p << " + e / " << per << ");\n";
         break;
       case IN_ONEHOT:
@@ -290,33 +387,59 @@ void Graph::emit_ew_group(int r, const int* seed_ptr,
              << ") == e % " << per << ") ? 1.f : 0.f;\n";
         break;
       default: {  // IN_STRIDED: row-major coordinates of e, dotted with the operand's strides
-        lane << "      i64 o" << s << " = 0;\n      { i64 rem = e;\n";
+        lane << "      i64 o" << si << " = 0;\n      { i64 rem = e;\n";
         for (int d = R - 1; d >= 0; --d) {
           if (os[d] == 1) continue;
           if (in.strides[d] != 0)
-            lane << "        o" << s << " += (rem % " << os[d] << "ll) * " << in.strides[d] << "ll;\n";
+            lane << "        o" << si << " += (rem % " << os[d] << "ll) * " << in.strides[d] << "ll;\n";
           if (d > 0) lane << "        rem /= " << os[d] << "ll;\n";
         }
-        lane << "      }\n      const float " << x << " = __ldg(" << p << " + o" << s << ");\n";
+        lane << "      }\n      const float " << x << " = __ldg(" << p << " + o" << si << ");\n";
       }
     }
   }
 
   std::ostringstream k;
   k << "(";
-  for (size_t s = 0; s < ins.size(); ++s) k << "const float* __restrict__ p" << s << ", ";
+  for (size_t si = 0; si < ins.size(); ++si) k << "const float* __restrict__ p" << si << ", ";
   k << "float* __restrict__ out, const int* __restrict__ seedp, i64 drop_off) {\n";
   k << "  const u32 seed = " << (has_drop ? "seedp ? (u32)(*seedp) : 0u" : "0u") << ";\n";
   k << "  (void)seed; (void)drop_off;\n";
-  if (vec) {
+  int64_t nchunk = 1;
+  const std::string L = std::to_string(len) + "ll";
+  if (rs == RED_ROW) {
+    // one warp per row; lanes sum j = lane, lane + 32, ... then a shuffle tree
+    // (the unfused row kernel's order)
+    const bool mean = P.kind[G.red] == "mean_last";
+    k << "  const int lane = threadIdx.x & 31;\n  const i64 nw = ((i64)gridDim.x * 256) >> 5;\n";
+    k << "  for (i64 r = (((i64)blockIdx.x * 256 + threadIdx.x) >> 5); r < " << rows << "ll; r += nw) {\n";
+    k << "    float acc = 0.f;\n    for (i64 j = lane; j < " << L << "; j += 32) {\n      const i64 e = r * " << L
+      << " + j;\n";
+    k << lane.str() << ops.str() << "      acc += " << value << ";\n    }\n";
+    k << "    for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);\n";
+    k << "    if (lane == 0) out[r] = " << (mean ? "__fdiv_rn(acc, " + lit((float)len) + ")" : "acc") << ";\n  }\n}\n";
+  } else if (rs == RED_COL) {
+    // first pass of the deterministic column sum: rows of chunk blockIdx.y in
+    // ascending order (the unfused kernel's order); the fold is shared
+    nchunk = colsum_chunks(rows, len);
+    if (nchunk > 1 && (!scratch || scratch_floats < (size_t)(nchunk * len)))
+      throw TgError("Error", "internal: scratch too small for a fused column sum");
+    const int64_t rp = (rows + nchunk - 1) / nchunk;
+    k << "  const i64 col = (i64)blockIdx.x * 256 + threadIdx.x;\n  if (col >= " << L << ") return;\n";
+    k << "  const i64 r0 = (i64)blockIdx.y * " << rp << "ll;\n";
+    k << "  const i64 r1 = r0 + " << rp << "ll < " << rows << "ll ? r0 + " << rp << "ll : " << rows << "ll;\n";
+    k << "  float acc = 0.f;\n  for (i64 r = r0; r < r1; ++r) {\n      const i64 e = r * " << L << " + col;\n";
+    k << lane.str() << ops.str() << "      acc += " << value << ";\n  }\n";
+    k << "  out[(i64)blockIdx.y * " << L << " + col] = acc;\n}\n";
+  } else if (vec) {
     k << "  for (i64 t = (i64)blockIdx.x * 256 + threadIdx.x; t < " << n / 4 << "ll; t += (i64)gridDim.x * 256) {\n";
     k << "    const i64 i = t * 4;\n" << pre.str();
     k << "    float r[4];\n#pragma unroll\n    for (int l = 0; l < 4; ++l) {\n      const i64 e = i + l;\n";
-    k << lane.str() << ops.str() << "      r[l] = v" << o << ";\n    }\n";
+    k << lane.str() << ops.str() << "      r[l] = " << value << ";\n    }\n";
     k << "    *reinterpret_cast<float4*>(out + i) = make_float4(r[0], r[1], r[2], r[3]);\n  }\n}\n";
   } else {
     k << "  for (i64 e = (i64)blockIdx.x * 256 + threadIdx.x; e < " << n << "ll; e += (i64)gridDim.x * 256) {\n";
-    k << pre.str() << lane.str() << ops.str() << "      out[e] = v" << o << ";\n  }\n}\n";
+    k << pre.str() << lane.str() << ops.str() << "      out[e] = " << value << ";\n  }\n}\n";
   }
   std::string body = k.str();
   char name[40];
@@ -339,20 +462,35 @@ void Graph::emit_ew_group(int r, const int* seed_ptr,
   };
   auto A = std::make_shared<Args>();
   for (auto& in : ins) A->in.push_back(in.ptr);
-  A->out = out;
+  A->out = (rs == RED_COL && nchunk > 1) ? static_cast<void*>(scratch) : out;
   A->seed = seed_ptr;
   A->drop_off = (long long)ctx->rank * n;
-  const int64_t work = vec ? n / 4 : n;
-  int64_t blocks = (work + 255) / 256, cap = (int64_t)device_sm_count() * 8;
-  const unsigned grid = (unsigned)std::max<int64_t>(1, std::min(blocks, cap));
-  if (mem.size() > 1) label = "fused_ew|" + label.substr(0, 160);
-  add(label, [fn, A, grid](cudaStream_t s) {
+  const int64_t sms = device_sm_count();
+  unsigned gx = 1, gy = 1;
+  if (rs == RED_ROW) {
+    const int64_t blocks = (rows + 7) / 8;
+    gx = (unsigned)std::max<int64_t>(1, std::min(blocks, sms * 16));
+  } else if (rs == RED_COL) {
+    gx = (unsigned)((len + 255) / 256);
+    gy = (unsigned)nchunk;
+  } else {
+    const int64_t work = vec ? n / 4 : n;
+    const int64_t blocks = (work + 255) / 256;
+    gx = (unsigned)std::max<int64_t>(1, std::min(blocks, sms * 8));
+  }
+  if (G.red >= 0) label = "fused_red|" + P.kind[G.red] + ":" + label.substr(0, 150);
+  else if (G.members.size() > 1) label = "fused_ew|" + label.substr(0, 160);
+  float* fold_out = reinterpret_cast<float*>(out);
+  const int64_t fold_n = (rs == RED_COL && nchunk > 1) ? nchunk : 0, fold_len = len;
+  float* fold_part = scratch;
+  add(label, [fn, A, gx, gy, fold_n, fold_len, fold_part, fold_out](cudaStream_t s) {
     std::vector<void*> args;
     for (auto& p : A->in) args.push_back(const_cast<const void**>(&p));
     args.push_back(&A->out);
     args.push_back(const_cast<const int**>(&A->seed));
     args.push_back(&A->drop_off);
-    jit_launch(*fn, grid, 256, args.data(), s);
+    jit_launch(*fn, gx, gy, 256, args.data(), s);
+    if (fold_n > 0) launch_colsum_fold(fold_part, fold_out, fold_n, fold_len, s);
   });
 }
 

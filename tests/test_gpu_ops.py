@@ -199,3 +199,23 @@ def test_randn_and_categorical(ctx):
                                                                    "__prngSeed": seed}, rtol=1e-3)
     logits = rnd([16, 50], 33, -2, 2)
     run(ctx, lambda: tg.categorical(T("l", [16, 50])), {"l": logits, "__prngSeed": seed}, exact=True)
+
+
+def test_fused_reductions_and_shared_producers(ctx):
+    """Elementwise groups consumed by row and column reductions, and a cheap
+    producer recomputed by each of its consumers (the LayerNorm shapes)."""
+    x, y, m = rnd([256, 96], 71), rnd([96], 72), rnd([256, 1], 73)
+    run(ctx, lambda: tg.mean(tg.mul(T("x", [256, 96]), T("y", [96])), -1, keepDims=True), {"x": x, "y": y})
+    def square_sum():
+        xx = T("x", [256, 96])
+        return tg.sum(tg.mul(xx, xx), -1)
+    run(ctx, square_sum, {"x": x})
+    run(ctx, lambda: tg.sumToShape(tg.mulScalar(T("x", [256, 96]), 0.5), [96]), {"x": x})
+    big = rnd([4096, 96], 74)
+    run(ctx, lambda: tg.sumToShape(tg.mul(T("b", [4096, 96]), T("y", [96])), [1, 96]), {"b": big, "y": y})
+
+    def shared():
+        mm = T("m", [256, 1])
+        c = tg.sub(T("x", [256, 96]), mm)
+        return tg.add(tg.mul(c, c), tg.div(c, tg.sqrt(tg.addScalar(mm, 3.0))))
+    run(ctx, shared, {"x": x, "m": np.abs(m)})

@@ -100,3 +100,19 @@ def test_data_parallel_plan_adds_one_allreduce():
     assert k2.count("nccl_allreduce") == 1
     # the gradient allreduce precedes the fused optimizer pass
     assert k2.index("nccl_allreduce") < k2.index("adam_flat")
+
+
+def test_reduction_consumes_its_elementwise_producer():
+    g = trace_fn(lambda: tg.sum(tg.mul(T("x", [64, 48]), T("y", [48])), -1))
+    r = BK.plan_dry(_program(g, {}, [], g.outputs[0], None, len(g.ops)))
+    assert r["launches"] == ["fused_red|sum_last:mul"]
+
+
+def test_cheap_shared_producer_is_recomputed_by_each_consumer():
+    def f():
+        x = T("x", [64, 48])
+        c = tg.sub(x, T("m", [64, 1]))          # read by two consumers
+        return tg.add(tg.mul(c, c), tg.mulScalar(c, 0.5))
+    g = trace_fn(f)
+    r = BK.plan_dry(_program(g, {}, [], g.outputs[0], None, len(g.ops)))
+    assert len(r["launches"]) == 1 and r["launches"][0].startswith("fused_ew|")
