@@ -233,12 +233,17 @@ void Graph::plan_storage() {
   for (auto& g : P.grads) {
     int G = g.second;
     int64_t off = param_off_.at(g.first);
-    bool direct = views_[G].root == G && !views_[G].onehot && P.producer[G] >= 0 &&
-                  !is_leaf_kind(P.kind[P.producer[G]]) && !is_const_kind(P.kind[P.producer[G]]) &&
-                  loc_[G].arena < 0 && !grad_placed.count(G) && !op_done_[P.producer[G]];
+    // The gradient is usually a same-shape view (sum_to_shape, reshape) of
+    // the tensor its producer writes: place that root in the gradient slot.
+    const TView& vg = views_[G];
+    const int R = vg.onehot ? -1 : vg.root;
+    bool direct = R >= 0 && vg.off == 0 && vg.contiguous && P.T[R].numel == P.T[G].numel &&
+                  P.producer[R] >= 0 && !is_leaf_kind(P.kind[P.producer[R]]) &&
+                  !is_const_kind(P.kind[P.producer[R]]) && loc_[R].arena < 0 && !grad_placed.count(R) &&
+                  !op_done_[P.producer[R]] && !ew_is_absorbed(P.producer[R]);
     if (direct) {
-      place(G, AR_GRAD, off);
-      grad_placed.insert(G);
+      place(R, AR_GRAD, off);
+      grad_placed.insert(R);
     } else {
       grad_copy_.push_back({G, off});
       int r = views_[G].onehot ? views_[views_[G].onehot_idx].root : views_[G].root;

@@ -413,7 +413,7 @@ void Graph::emit_ew_group(int gi, const int* seed_ptr, float* scratch, size_t sc
     const bool mean = P.kind[G.red] == "mean_last";
     k << "  const int lane = threadIdx.x & 31;\n  const i64 nw = ((i64)gridDim.x * 256) >> 5;\n";
     k << "  for (i64 r = (((i64)blockIdx.x * 256 + threadIdx.x) >> 5); r < " << rows << "ll; r += nw) {\n";
-    k << "    float acc = 0.f;\n    for (i64 j = lane; j < " << L << "; j += 32) {\n      const i64 e = r * " << L
+    k << "    float acc = 0.f;\n#pragma unroll 4\n    for (i64 j = lane; j < " << L << "; j += 32) {\n      const i64 e = r * " << L
       << " + j;\n";
     k << lane.str() << ops.str() << "      acc += " << value << ";\n    }\n";
     k << "    for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);\n";
@@ -428,7 +428,7 @@ void Graph::emit_ew_group(int gi, const int* seed_ptr, float* scratch, size_t sc
     k << "  const i64 col = (i64)blockIdx.x * 256 + threadIdx.x;\n  if (col >= " << L << ") return;\n";
     k << "  const i64 r0 = (i64)blockIdx.y * " << rp << "ll;\n";
     k << "  const i64 r1 = r0 + " << rp << "ll < " << rows << "ll ? r0 + " << rp << "ll : " << rows << "ll;\n";
-    k << "  float acc = 0.f;\n  for (i64 r = r0; r < r1; ++r) {\n      const i64 e = r * " << L << " + col;\n";
+    k << "  float acc = 0.f;\n#pragma unroll 4\n  for (i64 r = r0; r < r1; ++r) {\n      const i64 e = r * " << L << " + col;\n";
     k << lane.str() << ops.str() << "      acc += " << value << ";\n  }\n";
     k << "  out[(i64)blockIdx.y * " << L << " + col] = acc;\n}\n";
   } else if (vec) {
