@@ -6,7 +6,9 @@
 //
 // Accuracy: each f32 operand x is split into hi = x with the low 13 mantissa
 // bits cleared (exactly representable in TF32) and lo = x - hi (exact in
-// f32, then truncated to TF32 by the tensor core). The product is
+// f32, then truncated to TF32 by the tensor core). kind::tf32 MMAs truncate
+// their f32 operands (they ignore the low 13 bits; checked on B200), so raw
+// f32 data serves as hi without being rewritten. The product is
 // accumulated as lo_a*hi_b + hi_a*lo_b + hi_a*hi_b; the dropped lo_a*lo_b
 // term and the truncation of lo are ~2^-20 relative.
 //
@@ -53,23 +55,30 @@ __device__ int g_gemm_tc_dbg[8];
 // Pipeline timeline of CTA (0,0,0) when TcParams::trace is set (SM clock
 // cycles): [0][it] TMA issued, [1][it] stage landed (split warps),
 // [2][it] split done, [3][it] MMAs issued, [4][c] chunk drained,
-// [5][0] start, [5][1] epilogue start, [5][2] epilogue end.
+// [5][0] start, [5][1] epilogue start, [5][2] epilogue end, [6..9][it] each
+// split warp done, [10][it] MMA warp saw the stage ready.
 constexpr int TC_TRACE_N = 64;
-__device__ long long g_gemm_tc_trace[6][TC_TRACE_N];
+__device__ long long g_gemm_tc_trace[12][TC_TRACE_N];
 
 constexpr int TC_BM = 128, TC_BN = 128, TC_BK = 32;
 constexpr int TC_TILE_BYTES = 128 * TC_BK * 4;  // 16 KB per operand tile
 // Per stage: [0] A as landed by TMA, [1] B hi (K-major MMA operand; TMA lands
 // a K-major B here and it is split in place), [2] B lo, [3] B as landed when
-// it is MN-major. A K-major B needs no slot 3, so its ring has four 48 KB
-// stages instead of three 64 KB ones: the same 192 KB, and a deeper pipeline
-// to hide the TMA latency (1.5-2.5K cycles) plus the split (about 1K).
-constexpr int TC_RING_BYTES = 12 * TC_TILE_BYTES;
-template <int NS> struct TcRing {
-  static constexpr int stage_bytes = TC_RING_BYTES / NS;
+// it is MN-major. Three stages hide the TMA latency (1.5-2.5K cycles) plus the
+// split (about 1K); a fourth measured no faster. A K-major B needs no slot 3,
+// and the 48 KB saved hold the whole output tile for the epilogue (one
+// staging pass instead of two).
+#ifndef TC_STAGES_BK
+#define TC_STAGES_BK 3
+#define TC_EPI_BK 4
+#endif
+template <bool BK> struct TcCfg {
+  static constexpr int stages = BK ? TC_STAGES_BK : 3;
+  static constexpr int stage_bytes = (BK ? 3 : 4) * TC_TILE_BYTES;
+  static constexpr int epi_tiles = BK ? TC_EPI_BK : 2;  // 32 x 128 output sub-tiles staged at once
+  static constexpr int ring_bytes = stages * stage_bytes;
+  static constexpr int smem = ring_bytes + epi_tiles * TC_TILE_BYTES + 1024 + 256;
 };
-constexpr int TC_EPI_BYTES = 2 * TC_TILE_BYTES;  // output staging: half a tile at a time
-constexpr int TC_SMEM = TC_RING_BYTES + TC_EPI_BYTES + 1024 + 256;
 constexpr uint32_t TC_TMEM_COLS = 512;
 constexpr uint32_t TC_ACOL = 2 * TC_BN;  // first TMEM column of the per-stage A hi/lo (64 columns each)
 constexpr long long TC_SPIN_LIMIT = 1ll << 22;
@@ -240,12 +249,13 @@ __device__ __forceinline__ void split_a_row(const uint8_t* a, int r, bool kmajor
         v[kk] = *reinterpret_cast<const float*>(box + k * 128 + ((((m >> 2) ^ (k & 7))) << 4) + ((m & 3) << 2));
       }
     }
+    // hi: the raw f32 bits (the MMA truncates them to TF32); lo: the remainder
     uint32_t w[16];
 #pragma unroll
-    for (int e = 0; e < 16; ++e) w[e] = __float_as_uint(tf32_hi(v[e]));
+    for (int e = 0; e < 16; ++e) w[e] = __float_as_uint(v[e]);
     tmem_st16(tcol + 16 * h, w);
 #pragma unroll
-    for (int e = 0; e < 16; ++e) w[e] = __float_as_uint(v[e] - __uint_as_float(w[e]));
+    for (int e = 0; e < 16; ++e) w[e] = __float_as_uint(v[e] - tf32_hi(v[e]));
     tmem_st16(tcol + 32 + 16 * h, w);
   }
 }
@@ -255,17 +265,15 @@ __device__ __forceinline__ void split_b(uint8_t* st, int t, bool kmajor) {
   uint8_t* hi_t = st + TC_TILE_BYTES;
   uint8_t* lo_t = st + 2 * TC_TILE_BYTES;
   if (kmajor) {
-    // landed K-major in slot 1: split in place, lo into slot 2 (same layout)
-    float4* hi = reinterpret_cast<float4*>(hi_t);
+    // Landed K-major in slot 1, which the MMA reads as hi unchanged: kind::tf32
+    // MMAs ignore the low 13 mantissa bits of their f32 operands (truncation,
+    // checked on B200), so only lo goes to slot 2 (same layout).
+    const float4* raw = reinterpret_cast<const float4*>(hi_t);
     float4* lo = reinterpret_cast<float4*>(lo_t);
-#pragma unroll 4
+#pragma unroll 8
     for (int q = t; q < TC_TILE_BYTES / 16; q += 128) {
-      const float4 x = hi[q];
-      float4 h, l;
-      h.x = tf32_hi(x.x); h.y = tf32_hi(x.y); h.z = tf32_hi(x.z); h.w = tf32_hi(x.w);
-      l.x = x.x - h.x; l.y = x.y - h.y; l.z = x.z - h.z; l.w = x.w - h.w;
-      hi[q] = h;
-      lo[q] = l;
+      const float4 x = raw[q];
+      lo[q] = make_float4(x.x - tf32_hi(x.x), x.y - tf32_hi(x.y), x.z - tf32_hi(x.z), x.w - tf32_hi(x.w));
     }
   } else {
     // Landed MN-major in slot 3: 4 boxes (N chunk j) of 32 K-rows x 128
@@ -307,19 +315,21 @@ __device__ __forceinline__ void split_b(uint8_t* st, int t, bool kmajor) {
 // Persistent: each CTA walks units blockIdx.x, blockIdx.x + gridDim.x, ...;
 // the stage ring, the accumulator pair and every barrier phase continue
 // across units, so one unit's epilogue overlaps the next unit's main loop.
-template <int NS>
+template <bool BK>
 __global__ void __launch_bounds__(448, 1) gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA,
                                                          const __grid_constant__ CUtensorMap tmB,
                                                          const __grid_constant__ CUtensorMap tmC,
                                                          const __grid_constant__ TcParams P) {
-  constexpr int SB = TcRing<NS>::stage_bytes;
+  constexpr int NS = TcCfg<BK>::stages;
+  constexpr int SB = TcCfg<BK>::stage_bytes;
+  constexpr int ET = TcCfg<BK>::epi_tiles;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   // 1 KB-aligned base for the 128B-swizzled tiles. Offsetting the shared
   // array (rather than casting through an integer) keeps the pointer in the
   // shared address space, so tile accesses compile to shared loads/stores.
   uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
-  uint8_t* epi = smem + TC_RING_BYTES;  // two output sub-tiles
-  uint64_t* full = reinterpret_cast<uint64_t*>(epi + TC_EPI_BYTES);
+  uint8_t* epi = smem + TcCfg<BK>::ring_bytes;  // ET output sub-tiles
+  uint64_t* full = reinterpret_cast<uint64_t*>(epi + ET * TC_TILE_BYTES);
   uint64_t* conv = full + NS;
   uint64_t* empty = conv + NS;
   uint64_t* dfull = empty + NS;   // [2] accumulator chunk finished (MMA commit)
@@ -393,13 +403,13 @@ __global__ void __launch_bounds__(448, 1) gemm_tc_kernel(const __grid_constant__
         const TcUnit U = tc_unit(P, u);
         for (int it = 0; it < U.nk; ++it, ++gs) {
           const int s = gs % NS;
-          const uint32_t ph = (uint32_t)(gs / NS) & 1u;
           const int c = gc + it / TC_CHUNK, acc = c & 1;
           const bool chunk_start = (it % TC_CHUNK) == 0;
           if (chunk_start && c >= 2 && !mbar_wait(&dempty[acc], (uint32_t)((c - 2) >> 1) & 1u, 5)) {
             ok = false; break;
           }
-          if (!mbar_wait(&conv[s], ph, 2)) { ok = false; break; }
+          if (!mbar_wait(&conv[s], (uint32_t)(gs / NS) & 1u, 2)) { ok = false; break; }
+          mark(10, gs);
           asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
           const uint32_t base = smem_u32(smem + s * SB);
           const uint32_t b_hi = base + TC_TILE_BYTES, b_lo = base + 2 * TC_TILE_BYTES;
@@ -428,22 +438,27 @@ __global__ void __launch_bounds__(448, 1) gemm_tc_kernel(const __grid_constant__
     const int t = threadIdx.x - 64;  // 0..127
     const int r = (warp & 3) * 32 + lane;
     const uint32_t lane_base = (uint32_t)((warp & 3) * 32) << 16;
+    // After a failed wait these threads skip the data work but keep the
+    // named barrier, so none is left waiting at it.
     int gs = 0;
-    for (int64_t u = blockIdx.x; u < P.units && ok; u += gridDim.x) {
+    for (int64_t u = blockIdx.x; u < P.units; u += gridDim.x) {
       const TcUnit U = tc_unit(P, u);
       for (int it = 0; it < U.nk; ++it, ++gs) {
         const int s = gs % NS;
         const uint32_t ph = (uint32_t)(gs / NS) & 1u;
-        if (!mbar_wait(&full[s], ph, 3)) { ok = false; break; }
+        if (ok && !mbar_wait(&full[s], ph, 3)) ok = false;
         if (t == 0) mark(1, gs);
         uint8_t* st = smem + s * SB;
-        split_a_row(st, r, P.a_kmajor != 0, tmem + lane_base + TC_ACOL + 64u * (uint32_t)s);
-        split_b(st, t, P.b_kmajor != 0);
+        if (ok) {
+          split_a_row(st, r, P.a_kmajor != 0, tmem + lane_base + TC_ACOL + 64u * (uint32_t)s);
+          split_b(st, t, P.b_kmajor != 0);
+        }
         asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
         asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
         mbar_arrive(&conv[s]);
         if (t == 0) mark(2, gs);
+        if (lane == 0) mark(6 + (t >> 5), gs);
         if (t == 0 && blockIdx.x == 0) g_gemm_tc_dbg[1] = gs + 1;
       }
     }
@@ -499,34 +514,35 @@ __global__ void __launch_bounds__(448, 1) gemm_tc_kernel(const __grid_constant__
                          : P.C + (int64_t)U.i1 * P.c_batch + (int64_t)U.i2 * P.c_batch2;
       if (P.tma_store) {
         const float brow = (bias && bias_m && U.m0 + r < P.M) ? bias[U.m0 + r] : 0.f;
+        // sub-tile j (0..3) is staged in phase j / ET, in slot j % ET
 #pragma unroll
-        for (int h = 0; h < 2; ++h) {
+        for (int h = 0; h < 4 / ET; ++h) {
           // the previous TMA store must be done reading the staging buffer
           if (e == 0) asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
           asm volatile("bar.sync 2, 256;" ::: "memory");
           if (ok) {
             if (!colmaj) {
-              // half h = sub-tiles 2h, 2h+1 = the columns held by the hh == h warps
-              if (hh == h) {
+              // sub-tile j = tile columns 32j..32j+31, held by the hh == j / 2 warps
 #pragma unroll
-                for (int jj = 0; jj < 2; ++jj) {
+              for (int jj = 0; jj < 2; ++jj) {
+                const int j = 2 * hh + jj;
+                if (j / ET != h) continue;
+                uint8_t* sub = epi + (j % ET) * TC_TILE_BYTES;
 #pragma unroll
-                  for (int c = 0; c < 8; ++c) {
-                    float v[4];
+                for (int c = 0; c < 8; ++c) {
+                  float v[4];
 #pragma unroll
-                    for (int q = 0; q < 4; ++q) {
-                      const int j = 32 * jj + 4 * c + q;
-                      v[q] = sum[j] * alpha + brow;
-                      if (bias && !bias_m && U.n0 + cb + j < P.N) v[q] += bias[U.n0 + cb + j];
-                    }
-                    *reinterpret_cast<float4*>(epi + jj * TC_TILE_BYTES + r * 128 + ((c ^ (r & 7)) << 4)) =
-                        make_float4(v[0], v[1], v[2], v[3]);
+                  for (int q = 0; q < 4; ++q) {
+                    const int jc = 32 * jj + 4 * c + q;
+                    v[q] = sum[jc] * alpha + brow;
+                    if (bias && !bias_m && U.n0 + cb + jc < P.N) v[q] += bias[U.n0 + cb + jc];
                   }
+                  *reinterpret_cast<float4*>(sub + r * 128 + ((c ^ (r & 7)) << 4)) = make_float4(v[0], v[1], v[2], v[3]);
                 }
               }
-            } else if ((r >> 6) == h) {
-              // half h = sub-tiles of tile rows 64h..64h+63, every column line
-              uint8_t* sub = epi + ((r >> 5) & 1) * TC_TILE_BYTES + ((r & 3) << 2);
+            } else if ((r >> 5) / ET == h) {
+              // sub-tile j = tile rows 32j..32j+31, every column line
+              uint8_t* sub = epi + ((r >> 5) % ET) * TC_TILE_BYTES + ((r & 3) << 2);
               const int mc = (r & 31) >> 2;
 #pragma unroll
               for (int j = 0; j < 64; ++j) {
@@ -545,9 +561,9 @@ __global__ void __launch_bounds__(448, 1) gemm_tc_kernel(const __grid_constant__
             const int64_t inner0 = colmaj ? U.m0 : U.n0, inner_n = colmaj ? P.M : P.N;
             const int outer0 = (int)(colmaj ? U.n0 : U.m0);
 #pragma unroll
-            for (int jj = 0; jj < 2; ++jj) {
-              const int64_t i0 = inner0 + 32 * (2 * h + jj);
-              if (i0 < inner_n) tma_store_4d(&tmC, epi + jj * TC_TILE_BYTES, (int)i0, outer0, z2, z3);
+            for (int sl = 0; sl < ET; ++sl) {
+              const int64_t i0 = inner0 + 32 * (h * ET + sl);
+              if (i0 < inner_n) tma_store_4d(&tmC, epi + sl * TC_TILE_BYTES, (int)i0, outer0, z2, z3);
             }
             asm volatile("cp.async.bulk.commit_group;" ::: "memory");
           }
@@ -735,16 +751,18 @@ bool launch_gemm_tc(const GemmDesc& g, cudaStream_t s) {
 
   static bool attr = false;
   if (!attr) {
-    if (cudaFuncSetAttribute(gemm_tc_kernel<3>, cudaFuncAttributeMaxDynamicSharedMemorySize, TC_SMEM) != cudaSuccess ||
-        cudaFuncSetAttribute(gemm_tc_kernel<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, TC_SMEM) != cudaSuccess)
+    if (cudaFuncSetAttribute(gemm_tc_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             TcCfg<true>::smem) != cudaSuccess ||
+        cudaFuncSetAttribute(gemm_tc_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             TcCfg<false>::smem) != cudaSuccess)
       return false;
     attr = true;
   }
   p.units = ((N + TC_BN - 1) / TC_BN) * ((M + TC_BM - 1) / TC_BM) * g.batch * splits;
   const int64_t sms = device_sm_count();
   const unsigned grid = (unsigned)(p.units < sms ? p.units : sms);
-  if (bk) gemm_tc_kernel<4><<<grid, 448, TC_SMEM, s>>>(ta, tb, tc, p);
-  else gemm_tc_kernel<3><<<grid, 448, TC_SMEM, s>>>(ta, tb, tc, p);
+  if (bk) gemm_tc_kernel<true><<<grid, 448, TcCfg<true>::smem, s>>>(ta, tb, tc, p);
+  else gemm_tc_kernel<false><<<grid, 448, TcCfg<false>::smem, s>>>(ta, tb, tc, p);
   if (splits > 1) {
     int64_t total = g.batch * M * N;
     int64_t blocks = (total + 255) / 256, cap = (int64_t)device_sm_count() * 8;
@@ -758,7 +776,7 @@ int gemm_tc_debug(int* out8) {
 }
 
 int gemm_tc_trace(long long* out, int cap) {
-  const int n = 6 * TC_TRACE_N;
+  const int n = 12 * TC_TRACE_N;
   if (cap < n) return -1;
   return cudaMemcpyFromSymbol(out, g_gemm_tc_trace, n * sizeof(long long)) == cudaSuccess ? n : -1;
 }
