@@ -84,6 +84,14 @@ bool broadcasts_to(const std::vector<int64_t>& a, const std::vector<int64_t>& b)
   return true;
 }
 
+// Ops that cost tens of instructions per element (SFU sequences, IEEE
+// division): worth computing once per value rather than once per broadcast
+// element.
+bool expensive_kind(const std::string& k) {
+  return k == "sqrt" || k == "rsqrt" || k == "div" || k == "exp" || k == "log" || k == "tanh" ||
+         k == "sigmoid" || k == "erf" || k == "sin" || k == "cos";
+}
+
 constexpr int kMaxGroupInputs = 12;
 constexpr int kMaxGroupOps = 48;
 
@@ -190,6 +198,13 @@ void Graph::plan_fusion() {
       if (P.T[t].shape != P.T[P.out[i]].shape &&
           (!broadcasts_to(P.T[t].shape, P.T[P.out[i]].shape) || posdep[p]))
         continue;
+      // a broadcast producer is recomputed for every element it is read at:
+      // keep expensive row-level values (sqrt, division, ...) materialised
+      if (P.T[t].numel * 8 <= P.T[P.out[i]].numel) {
+        bool costly = false;
+        for (int m : mem[p]) costly = costly || expensive_kind(P.kind[m]);
+        if (costly) continue;
+      }
       const auto& cs = P.consumers[t];
       if (cs.size() == 1) {
         // sole consumer: the producer's group moves into this one
