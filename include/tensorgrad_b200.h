@@ -73,10 +73,13 @@ int tg_upload_params(tg_ctx* ctx, int graph_id, int n, const char* const* names,
                      const size_t* numel);
 int tg_download_params(tg_ctx* ctx, int graph_id, int n, const char* const* names, float* const* out,
                        const size_t* numel);
-/* One synchronous training step from host inputs: H2D, kernels, loss D2H. */
+/* One synchronous training step from host inputs: H2D, kernels, loss D2H.
+ * Every declared input must be given (the runtime-written PRNG seed and
+ * optimizer scalars excepted), each with its exact byte size. */
 int tg_step(tg_ctx* ctx, int graph_id, int n, const char* const* names, const void* const* data,
             const size_t* bytes, float* loss_out, void* const* capture_out);
-/* One forward run: output (and captures) copied into caller buffers. */
+/* One forward run: output (and captures) copied into caller buffers. Same
+ * input rules as tg_step. */
 int tg_run(tg_ctx* ctx, int graph_id, int n, const char* const* names, const void* const* data,
            const size_t* bytes, void* output_out, void* const* capture_out);
 /* Split step: copy inputs (device_src != 0: data are device pointers),
@@ -87,6 +90,17 @@ int tg_launch_step(tg_ctx* ctx, int graph_id);
 int tg_read_loss(tg_ctx* ctx, int graph_id, float* loss_out);
 int tg_stream(tg_ctx* ctx, void** stream_out);
 int tg_reset_optimizer(tg_ctx* ctx, int graph_id);
+/* Optimizer state by state name (adam_m_<param>, adam_v_<param>,
+ * sgd_v_<param>), strict like the param calls; with tg_get_counters /
+ * tg_set_counters (optimizer steps taken, PRNG seed counter) this is the
+ * training checkpoint. New: the reference exports no optimizer state and its
+ * reset re-initialises it (src/compile.ts:641-657; src/runtime.ts:461-465). */
+int tg_upload_states(tg_ctx* ctx, int graph_id, int n, const char* const* names, const float* const* data,
+                     const size_t* numel);
+int tg_download_states(tg_ctx* ctx, int graph_id, int n, const char* const* names, float* const* out,
+                       const size_t* numel);
+int tg_get_counters(tg_ctx* ctx, int graph_id, int64_t* step, int64_t* prng);
+int tg_set_counters(tg_ctx* ctx, int graph_id, int64_t step, int64_t prng);
 int tg_set_lr(tg_ctx* ctx, int graph_id, const char* lr_json, size_t len);
 int tg_destroy_graph(tg_ctx* ctx, int graph_id);
 int tg_read_grad(tg_ctx* ctx, int graph_id, const char* name, float* out);

@@ -18,3 +18,4 @@ from .dce import eliminateDeadCode
 from .optim import appendAdam, appendSGD, adamStepScalars
 from .shape import ShapeError
 from .compile import compile, compileForward, trace, CompiledTraining, CompiledForward  # noqa: A004
+from .safetensors import loadSafetensors, saveSafetensors

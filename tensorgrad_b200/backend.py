@@ -19,7 +19,8 @@ _lib = None
 
 EXPORTED = [
     "tg_nccl_unique_id", "tg_ctx_create", "tg_ctx_destroy", "tg_graph_create", "tg_graph_info",
-    "tg_upload_params", "tg_download_params", "tg_step", "tg_run", "tg_set_inputs", "tg_launch_step",
+    "tg_upload_params", "tg_download_params", "tg_upload_states", "tg_download_states", "tg_get_counters",
+    "tg_set_counters", "tg_step", "tg_run", "tg_set_inputs", "tg_launch_step",
     "tg_read_loss", "tg_stream", "tg_reset_optimizer", "tg_set_lr", "tg_destroy_graph", "tg_read_grad",
     "tg_read_tensor", "tg_launch_list", "tg_profile_step", "tg_debug_gemm_error", "tg_debug_gemm_dbg", "tg_debug_gemm_trace", "tg_colsum_noalloc", "tg_plan_dry", "tg_last_error_name", "tg_last_error_message",
 ]
@@ -63,6 +64,10 @@ def load(path: str = LIB_PATH):
         "tg_launch_list": [vp, ip, C.c_char_p, sz, szp],
         "tg_upload_params": [vp, ip, ip, cpp, vpp, szp],
         "tg_download_params": [vp, ip, ip, cpp, vpp, szp],
+        "tg_upload_states": [vp, ip, ip, cpp, vpp, szp],
+        "tg_download_states": [vp, ip, ip, cpp, vpp, szp],
+        "tg_get_counters": [vp, ip, C.POINTER(C.c_int64), C.POINTER(C.c_int64)],
+        "tg_set_counters": [vp, ip, C.c_int64, C.c_int64],
         "tg_step": [vp, ip, ip, cpp, vpp, szp, C.POINTER(C.c_float), vpp],
         "tg_run": [vp, ip, ip, cpp, vpp, szp, vp, vpp],
         "tg_set_inputs": [vp, ip, ip, cpp, vpp, szp, ip],
@@ -205,6 +210,30 @@ class DeviceGraph:
         sizes = (C.c_size_t * len(outs))(*[a.size for a in outs])
         _check(self.lib.tg_download_params(self.ctx.h, self.id, len(names), _names(names), ptrs, sizes))
         return dict(zip(names, outs))
+
+    def upload_states(self, states: Dict[str, np.ndarray]) -> None:
+        names = list(states)
+        arrs = [np.ascontiguousarray(states[n], dtype=np.float32).reshape(-1) for n in names]
+        ptrs = (C.c_void_p * len(arrs))(*[a.ctypes.data for a in arrs])
+        sizes = (C.c_size_t * len(arrs))(*[a.size for a in arrs])
+        _check(self.lib.tg_upload_states(self.ctx.h, self.id, len(names), _names(names), ptrs, sizes))
+
+    def download_states(self, shapes: Dict[str, tuple]) -> Dict[str, np.ndarray]:
+        names = list(shapes)
+        outs = [np.empty(shapes[n], np.float32) for n in names]
+        ptrs = (C.c_void_p * len(outs))(*[a.ctypes.data for a in outs])
+        sizes = (C.c_size_t * len(outs))(*[a.size for a in outs])
+        _check(self.lib.tg_download_states(self.ctx.h, self.id, len(names), _names(names), ptrs, sizes))
+        return dict(zip(names, outs))
+
+    def counters(self):
+        """(optimizer steps taken, PRNG seed counter)."""
+        a, b = C.c_int64(), C.c_int64()
+        _check(self.lib.tg_get_counters(self.ctx.h, self.id, C.byref(a), C.byref(b)))
+        return a.value, b.value
+
+    def set_counters(self, step: int, prng: int) -> None:
+        _check(self.lib.tg_set_counters(self.ctx.h, self.id, int(step), int(prng)))
 
     # -- steps ------------------------------------------------------------
     def _pack(self, inputs: Dict[str, np.ndarray]):

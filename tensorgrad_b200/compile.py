@@ -16,6 +16,7 @@ Results follow the reference's discriminated unions: ``step`` returns
 from __future__ import annotations
 
 import copy
+import json
 import random
 from collections import OrderedDict
 from typing import Callable, Dict, Optional
@@ -29,7 +30,10 @@ from .ir import Graph, graph_to_wire
 from .lr import rebaseLR
 from .module import Module, cloneModule, materializeParams, mulberry32
 from .optim import appendAdam, appendSGD
+from .safetensors import loadSafetensors, saveSafetensors
 from .trace import tensor_input, trace_fn
+
+CHECKPOINT_FORMAT = "tensorgrad_b200.checkpoint.v1"
 
 
 def _normalize_decl(d):
@@ -279,15 +283,53 @@ class CompiledTraining:
     def downloadParams(self) -> Dict[str, np.ndarray]:
         return self.device_graph.download_params(self.param_shapes)
 
-    def reset(self) -> None:
-        """Re-init params from the seed and zero optimizer state (src/compile.ts:641-657)."""
-        self.device_graph.upload_params(initial_params(self.graph, self.ir.materialized.initFns, self.seed))
-        self.device_graph.reset_optimizer()
-        self.steps_done = 0
+    def reset(self, opts: Optional[dict] = None) -> None:
+        """Re-init params from the seed and/or zero the optimizer state and its
+        step counter; both by default (src/compile.ts:641-657,
+        src/worker.ts:294-302). The dropout counter keeps running, as in the
+        reference, so a reset run draws fresh masks."""
+        opts = opts or {}
+        if opts.get("params", True):
+            self.device_graph.upload_params(initial_params(self.graph, self.ir.materialized.initFns, self.seed))
+        if opts.get("optimizer", True):
+            self.device_graph.reset_optimizer()
+            self.steps_done = 0
 
     def setLR(self, lr) -> None:
         """New schedule whose step 1 is the next step (src/worker.ts:304-319)."""
         self.device_graph.set_lr(rebaseLR(lr, self.steps_done + 1))
+
+    def exportCheckpoint(self) -> bytes:
+        """Params, optimizer state (m, v or velocity per param) and the step and
+        PRNG counters as one safetensors blob: resuming from it continues the
+        run exactly. New: the reference exports only params."""
+        params = self.downloadParams()
+        shapes = {n: self.graph.tensors[st["tensor"]].shape for n, st in self.program["states"].items()}
+        states = self.device_graph.download_states(shapes)
+        step, prng = self.device_graph.counters()
+        tensors = {f"param/{n}": v for n, v in params.items()}
+        tensors.update({f"state/{n}": v for n, v in states.items()})
+        meta = {"format": CHECKPOINT_FORMAT, "step": step, "prng": prng, "steps_done": self.steps_done,
+                "optimizer": json.dumps(self.optimizer, default=str)}
+        return saveSafetensors(tensors, meta)
+
+    def importCheckpoint(self, buf: bytes) -> None:
+        """Restore a blob from exportCheckpoint (strict: every param and
+        state of this model, nothing else)."""
+        d = loadSafetensors(buf)
+        meta = d["metadata"]
+        if meta.get("format") != CHECKPOINT_FORMAT:
+            raise BK.TgError("Error", "importCheckpoint: not a tensorgrad_b200 checkpoint")
+        params = {n[len("param/"):]: v for n, v in d["tensors"].items() if n.startswith("param/")}
+        states = {n[len("state/"):]: v for n, v in d["tensors"].items() if n.startswith("state/")}
+        want = set(self.program["states"])
+        if set(states) != want:
+            raise BK.TgError("Error", f"importCheckpoint: states {sorted(set(states) ^ want)} do not match the model")
+        self.uploadParams(params)
+        if states:
+            self.device_graph.upload_states(states)
+        self.device_graph.set_counters(int(meta["step"]), int(meta["prng"]))
+        self.steps_done = int(meta.get("steps_done", meta["step"]))
 
     def replaceModel(self, model) -> None:
         self.device_graph.destroy()

@@ -159,10 +159,35 @@ int tg_download_params(tg_ctx* ctx, int graph_id, int n, const char* const* name
   return guarded([&] { get_graph(ctx, graph_id)->download_params(n, names, out, numel); });
 }
 
+int tg_upload_states(tg_ctx* ctx, int graph_id, int n, const char* const* names, const float* const* data,
+                     const size_t* numel) {
+  return guarded([&] { get_graph(ctx, graph_id)->upload_states(n, names, data, numel); });
+}
+
+int tg_download_states(tg_ctx* ctx, int graph_id, int n, const char* const* names, float* const* out,
+                       const size_t* numel) {
+  return guarded([&] { get_graph(ctx, graph_id)->download_states(n, names, out, numel); });
+}
+
+int tg_get_counters(tg_ctx* ctx, int graph_id, int64_t* step, int64_t* prng) {
+  return guarded([&] {
+    if (!step || !prng) throw tg::TgError("Error", "tg_get_counters: null output");
+    get_graph(ctx, graph_id)->get_counters(step, prng);
+  });
+}
+
+int tg_set_counters(tg_ctx* ctx, int graph_id, int64_t step, int64_t prng) {
+  return guarded([&] {
+    if (step < 0 || prng < 0) throw tg::TgError("Error", "tg_set_counters: negative counter");
+    get_graph(ctx, graph_id)->set_counters(step, prng);
+  });
+}
+
 int tg_step(tg_ctx* ctx, int graph_id, int n, const char* const* names, const void* const* data,
             const size_t* bytes, float* loss_out, void* const* capture_out) {
   return guarded([&] {
     tg::Graph* g = get_graph(ctx, graph_id);
+    g->require_inputs(n, names);
     g->set_inputs(n, names, data, bytes, false);
     g->launch_step();
     g->read_loss(loss_out);
@@ -174,6 +199,7 @@ int tg_run(tg_ctx* ctx, int graph_id, int n, const char* const* names, const voi
            const size_t* bytes, void* output_out, void* const* capture_out) {
   return guarded([&] {
     tg::Graph* g = get_graph(ctx, graph_id);
+    g->require_inputs(n, names);
     g->set_inputs(n, names, data, bytes, false);
     g->launch_step();
     g->read_output(output_out);

@@ -132,6 +132,7 @@ class Graph {
   void upload_params(int n, const char* const* names, const float* const* data, const size_t* numel);
   void download_params(int n, const char* const* names, float* const* out, const size_t* numel);
   void set_inputs(int n, const char* const* names, const void* const* data, const size_t* bytes, bool device_src);
+  void require_inputs(int n, const char* const* names) const;
   void launch_step();  // enqueue one step (scalars + kernels), no sync
   void read_loss(float* out);
   void read_output(void* out);
@@ -139,6 +140,12 @@ class Graph {
   void read_tensor(int t, void* out);
   void read_grad(const std::string& name, float* out);
   void reset_optimizer();
+  void upload_states(int n, const char* const* names, const float* const* data, const size_t* numel);
+  void download_states(int n, const char* const* names, float* const* out, const size_t* numel);
+  int state_tensor(const std::string& name) const;
+  // Per-step counters: optimizer steps taken and the PRNG seed counter.
+  void get_counters(int64_t* step, int64_t* prng) const { *step = t_; *prng = prng_; }
+  void set_counters(int64_t step, int64_t prng) { t_ = step; prng_ = prng; }
   void set_lr(const char* lr_json, size_t len);
   std::string info_json() const;
   float* param_ptr(const std::string& name) const;

@@ -1057,6 +1057,22 @@ void Graph::read_grad(const std::string& name, float* out) {
   TG_CUDA(cudaStreamSynchronize(ctx->stream));
 }
 
+// Every declared input except those the runtime writes itself (the PRNG
+// seed and the optimizer's per-step scalars) must come with a step or a run
+// (src/runtime.ts:322-328).
+void Graph::require_inputs(int n, const char* const* names) const {
+  std::set<std::string> given(names, names + n), injected{"__prngSeed"};
+  if (P.optimizer) {
+    const auto& cfg = (*P.optimizer)["config"];
+    for (const char* k : {"lrtInputName", "decayShrinkInputName", "lrInputName"})
+      if (auto* v = cfg.find(k))
+        if (!v->is_null()) injected.insert(v->str());
+  }
+  for (const auto& kv : P.inputs)
+    if (!injected.count(kv.first) && !given.count(kv.first))
+      throw TgError("Error", "missing input '" + kv.first + "'");
+}
+
 void Graph::set_inputs(int n, const char* const* names, const void* const* data, const size_t* bytes,
                        bool device_src) {
   for (int i = 0; i < n; ++i) {
@@ -1090,6 +1106,38 @@ void Graph::download_params(int n, const char* const* names, float* const* out, 
     if ((int64_t)numel[i] != param_numel(names[i]))
       throw TgError("Error", std::string("downloadParams: size mismatch for '") + names[i] + "'");
     TG_CUDA(cudaMemcpyAsync(out[i], p, numel[i] * 4, cudaMemcpyDeviceToHost, ctx->stream));
+  }
+  TG_CUDA(cudaStreamSynchronize(ctx->stream));
+}
+
+// Optimizer state by name (adam_m_<param>, adam_v_<param>, sgd_v_<param>, or
+// any other state_input), for checkpoints.
+int Graph::state_tensor(const std::string& name) const {
+  for (auto& st : P.states)
+    if (st.name == name) return st.tensor;
+  return -1;
+}
+
+void Graph::upload_states(int n, const char* const* names, const float* const* data, const size_t* numel) {
+  for (int i = 0; i < n; ++i) {
+    const int t = state_tensor(names[i]);
+    if (t < 0 || loc_[views_[t].root].arena < 0)
+      throw TgError("Error", std::string("uploadState: unknown state '") + names[i] + "'");
+    if ((int64_t)numel[i] != P.T[t].numel)
+      throw TgError("Error", std::string("uploadState: size mismatch for '") + names[i] + "'");
+    TG_CUDA(cudaMemcpyAsync(ptr(t), data[i], numel[i] * 4, cudaMemcpyHostToDevice, ctx->stream));
+  }
+  TG_CUDA(cudaStreamSynchronize(ctx->stream));
+}
+
+void Graph::download_states(int n, const char* const* names, float* const* out, const size_t* numel) {
+  for (int i = 0; i < n; ++i) {
+    const int t = state_tensor(names[i]);
+    if (t < 0 || loc_[views_[t].root].arena < 0)
+      throw TgError("Error", std::string("downloadState: unknown state '") + names[i] + "'");
+    if ((int64_t)numel[i] != P.T[t].numel)
+      throw TgError("Error", std::string("downloadState: size mismatch for '") + names[i] + "'");
+    TG_CUDA(cudaMemcpyAsync(out[i], ptr(t), numel[i] * 4, cudaMemcpyDeviceToHost, ctx->stream));
   }
   TG_CUDA(cudaStreamSynchronize(ctx->stream));
 }
