@@ -157,6 +157,15 @@ def run_reference(args, w):
     print(json.dumps(line), flush=True)
 
 
+MODEL_DESC = {
+    "c1": "MLP 1-64-64-1 ReLU, Adam",
+    "c2": "CNN conv3x3 1-32, 32-64, maxpool, 9216-128-10, Adam",
+    "c3": "char MLP V27 ctx3 emb10 hidden200, SGD momentum",
+    "c4": "GPT V65 T256 d384 L6 H6 dropout0.2, AdamW",
+    "c5": "GPT V50304 T1024 d768 L12 H12, AdamW cosine",
+}
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -187,7 +196,9 @@ def main():
         dist.broadcast_object_list(obj, src=0)
         nccl_id = obj[0]
     ctx = BK.Context(local, rank, world, nccl_id)
-    per_rank = w.global_batch
+    # weak scaling: a fixed batch per rank. c5 names its global batch at 8 GPUs
+    # (256 = 32 per GPU), so its per-rank batch is 32 unless --batch says otherwise
+    per_rank = 32 if args.config == "c5" and not args.batch else w.global_batch
     gb = per_rank * world
     ir = build_training_ir(w.make_model(), w.loss, w.inputs(per_rank), w.optimizer)
     init = initial_params(ir.graph, ir.materialized.initFns, CF.PARAM_SEED)
@@ -265,16 +276,18 @@ def main():
 
     value = args.steps * gb / (ms * 1e-3)
     e2e = args.steps * gb / (e2e_ms * 1e-3)
-    line = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+    metric = METRIC if args.config == "c4" else f"train samples/sec ({w.name}, config {args.config[1:]})"
+    line = {"metric": metric, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "f32",
             "data": "synthetic (mulberry32 seed 1234 tokens, random-init params seed 42)",
-            "config": {"workload": w.name, "model": "GPT V65 T256 d384 L6 H6 dropout0.2", "global_batch": gb,
-                       "seq_len": 256, "parallelism": f"dp{world}",
+            "config": {"workload": w.name, "model": MODEL_DESC.get(args.config, w.name), "global_batch": gb,
+                       "per_rank_batch": per_rank, "seq_len": w.extra.get("T"), "parallelism": f"dp{world}",
                        "l2": "inputs and activations exceed L2 (126 MB) every step"},
             "e2e": {"value": e2e, "unit": UNIT, "h2d_bytes_per_step": in_bytes, "d2h_bytes_per_step": 4},
             "gpu_launches": len(kinds) * args.steps, "roofline": roof, "clocks": clk.summary(),
-            "loss": loss, "tokens_per_s": value * 256,
+            "loss": loss, "steps_per_s": args.steps / (ms * 1e-3),
+            "tokens_per_s": value * w.extra["T"] if "T" in w.extra else None,
             "tflops_algorithmic": w.flops_per_sample * value / 1e12}
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         v, dt = cpu_baseline(w, 2, os.cpu_count() or 1)
