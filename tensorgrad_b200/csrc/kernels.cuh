@@ -169,9 +169,15 @@ void launch_pick(const float* x, const int* t, float* out, int64_t rows, int64_t
 struct ConvDesc {
   int B, Cin, H, W, Cout, kH, kW, Hout, Wout, sH, sW, pH, pW, G;
 };
-void launch_conv2d(const ConvDesc& c, const float* x, const float* w, float* y, cudaStream_t s);
-void launch_conv2d_input_grad(const ConvDesc& c, const float* w, const float* dy, float* dx, cudaStream_t s);
-void launch_conv2d_weight_grad(const ConvDesc& c, const float* x, const float* dy, float* dw, cudaStream_t s);
+// conv2d and both gradients as column gathers plus GEMMs (kernels_conv.cu).
+// `which`: 0 forward, 1 input grad, 2 weight grad.
+int64_t conv_gemm_scratch_floats(const ConvDesc& c, int which);
+void launch_conv2d_gemm(const ConvDesc& c, const float* x, const float* w, float* y, float* scratch,
+                        int64_t scratch_floats, cudaStream_t s);
+void launch_conv2d_input_grad_gemm(const ConvDesc& c, const float* w, const float* dy, float* dx, float* scratch,
+                                   int64_t scratch_floats, cudaStream_t s);
+void launch_conv2d_weight_grad_gemm(const ConvDesc& c, const float* x, const float* dy, float* dw, float* scratch,
+                                    int64_t scratch_floats, cudaStream_t s);
 void launch_maxpool(const ConvDesc& c, const float* x, float* y, cudaStream_t s);
 void launch_maxpool_grad(const ConvDesc& c, const float* x, const float* dy, float* dx, cudaStream_t s);
 

@@ -3,7 +3,7 @@
 // Reference counterparts (one WGSL kernel per op there): permute
 // (src/codegen.ts:468-493), slice/scatter/concat (:715-819), broadcast_to
 // (:822-837), one_hot (:604-624), arange/const fills (:71-104), randn
-// (:212-239), conv2d + grads (:916-1093), max pool + grad (:1095-1185),
+// (:212-239), max pool + grad (:1095-1185); conv2d lives in kernels_conv.cu,
 // Adam (:841-905: three kernels plus three copy-backs per param there; one
 // in-place pass over flat arenas here).
 #include "kernels.cuh"
@@ -263,117 +263,6 @@ void launch_pick(const float* x, const int* t, float* out, int64_t rows, int64_t
 }
 
 // ------------------------------------------------------------- conv / pool --
-__global__ void __launch_bounds__(256) conv2d_kernel(const __grid_constant__ ConvDesc c, const float* __restrict__ x,
-                                                     const float* __restrict__ w, float* __restrict__ y) {
-  int64_t total = (int64_t)c.B * c.Cout * c.Hout * c.Wout;
-  int cpg = c.Cin / c.G, opg = c.Cout / c.G;
-  int64_t stride = (int64_t)gridDim.x * blockDim.x;
-  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += stride) {
-    int wo = i % c.Wout;
-    int ho = (i / c.Wout) % c.Hout;
-    int co = (i / ((int64_t)c.Wout * c.Hout)) % c.Cout;
-    int64_t b = i / ((int64_t)c.Wout * c.Hout * c.Cout);
-    int g = co / opg;
-    float s = 0.f;
-    for (int cl = 0; cl < cpg; ++cl) {
-      int ci = g * cpg + cl;
-      const float* xb = x + (b * c.Cin + ci) * c.H * c.W;
-      const float* wb = w + ((int64_t)co * cpg + cl) * c.kH * c.kW;
-      for (int kh = 0; kh < c.kH; ++kh) {
-        int hi = ho * c.sH + kh - c.pH;
-        if (hi < 0 || hi >= c.H) continue;
-        for (int kw = 0; kw < c.kW; ++kw) {
-          int wi = wo * c.sW + kw - c.pW;
-          if (wi < 0 || wi >= c.W) continue;
-          s = fmaf(xb[hi * c.W + wi], wb[kh * c.kW + kw], s);
-        }
-      }
-    }
-    y[i] = s;
-  }
-}
-void launch_conv2d(const ConvDesc& c, const float* x, const float* w, float* y, cudaStream_t s) {
-  conv2d_kernel<<<grid_for((int64_t)c.B * c.Cout * c.Hout * c.Wout, 256, 16), 256, 0, s>>>(c, x, w, y);
-}
-
-__global__ void __launch_bounds__(256) conv2d_dx_kernel(const __grid_constant__ ConvDesc c, const float* __restrict__ w,
-                                                        const float* __restrict__ dy, float* __restrict__ dx) {
-  int64_t total = (int64_t)c.B * c.Cin * c.H * c.W;
-  int cpg = c.Cin / c.G, opg = c.Cout / c.G;
-  int64_t stride = (int64_t)gridDim.x * blockDim.x;
-  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += stride) {
-    int wi = i % c.W;
-    int hi = (i / c.W) % c.H;
-    int ci = (i / ((int64_t)c.W * c.H)) % c.Cin;
-    int64_t b = i / ((int64_t)c.W * c.H * c.Cin);
-    int g = ci / cpg, cl = ci - g * cpg;
-    float s = 0.f;
-    for (int ol = 0; ol < opg; ++ol) {
-      int co = g * opg + ol;
-      const float* wb = w + ((int64_t)co * cpg + cl) * c.kH * c.kW;
-      const float* db = dy + (b * c.Cout + co) * c.Hout * c.Wout;
-      for (int kh = 0; kh < c.kH; ++kh) {
-        int nh = hi + c.pH - kh;
-        if (nh < 0 || nh % c.sH) continue;
-        int ho = nh / c.sH;
-        if (ho >= c.Hout) continue;
-        for (int kw = 0; kw < c.kW; ++kw) {
-          int nw = wi + c.pW - kw;
-          if (nw < 0 || nw % c.sW) continue;
-          int wo = nw / c.sW;
-          if (wo >= c.Wout) continue;
-          s = fmaf(wb[kh * c.kW + kw], db[ho * c.Wout + wo], s);
-        }
-      }
-    }
-    dx[i] = s;
-  }
-}
-void launch_conv2d_input_grad(const ConvDesc& c, const float* w, const float* dy, float* dx, cudaStream_t s) {
-  conv2d_dx_kernel<<<grid_for((int64_t)c.B * c.Cin * c.H * c.W, 256, 16), 256, 0, s>>>(c, w, dy, dx);
-}
-
-// Weight grad: one block per weight element, threads stride (b, ho, wo).
-__global__ void __launch_bounds__(256) conv2d_dw_kernel(const __grid_constant__ ConvDesc c, const float* __restrict__ x,
-                                                        const float* __restrict__ dy, float* __restrict__ dw) {
-  __shared__ float sm[8];
-  int cpg = c.Cin / c.G, opg = c.Cout / c.G;
-  int64_t nw = (int64_t)c.Cout * cpg * c.kH * c.kW;
-  int64_t red = (int64_t)c.B * c.Hout * c.Wout;
-  int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
-  for (int64_t e = blockIdx.x; e < nw; e += gridDim.x) {
-    int kw = e % c.kW;
-    int kh = (e / c.kW) % c.kH;
-    int cl = (e / ((int64_t)c.kW * c.kH)) % cpg;
-    int co = e / ((int64_t)c.kW * c.kH * cpg);
-    int ci = (co / opg) * cpg + cl;
-    float s = 0.f;
-    for (int64_t k = threadIdx.x; k < red; k += blockDim.x) {
-      int wo = k % c.Wout;
-      int ho = (k / c.Wout) % c.Hout;
-      int64_t b = k / ((int64_t)c.Wout * c.Hout);
-      int hi = ho * c.sH + kh - c.pH, wi = wo * c.sW + kw - c.pW;
-      if (hi < 0 || hi >= c.H || wi < 0 || wi >= c.W) continue;
-      s = fmaf(x[((b * c.Cin + ci) * c.H + hi) * c.W + wi], dy[((b * c.Cout + co) * c.Hout + ho) * c.Wout + wo], s);
-    }
-    for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
-    if (lane == 0) sm[wid] = s;
-    __syncthreads();
-    if (wid == 0) {
-      s = lane < 8 ? sm[lane] : 0.f;
-      for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
-      if (lane == 0) dw[e] = s;
-    }
-    __syncthreads();
-  }
-}
-void launch_conv2d_weight_grad(const ConvDesc& c, const float* x, const float* dy, float* dw, cudaStream_t s) {
-  int64_t nw = (int64_t)c.Cout * (c.Cin / c.G) * c.kH * c.kW;
-  int64_t cap = (int64_t)device_sm_count() * 16;
-  int64_t blocks = nw < cap ? nw : cap;
-  conv2d_dw_kernel<<<(unsigned)(blocks < 1 ? 1 : blocks), 256, 0, s>>>(c, x, dy, dw);
-}
-
 // Max pool with the reference's scan order and strict '>' from -3.4e38, so
 // the first maximum wins (test/_eval.ts:716-738).
 __global__ void maxpool_kernel(const __grid_constant__ ConvDesc c, const float* __restrict__ x, float* __restrict__ y) {

@@ -134,6 +134,30 @@ static int64_t scratch_for(const Program& P, int i, int action) {
     // either the batch folds into M (matmul) or stays a batch: same M*N*batch
     return 4 * std::max(gemm_tc_workspace_floats(M * batch, N, K, 1), gemm_tc_workspace_floats(M, N, K, batch));
   }
+  if (k == "conv2d" || k == "conv2d_input_grad" || k == "conv2d_weight_grad") {
+    const auto& O = P.op(i);
+    const auto& os = P.T[P.out[i]].shape;
+    ConvDesc c{};
+    c.sH = O["strideH"].i32(); c.sW = O["strideW"].i32(); c.pH = O["padH"].i32(); c.pW = O["padW"].i32();
+    c.G = O.find("groups") ? O["groups"].i32() : 1;
+    int which = 0;
+    if (k == "conv2d") {
+      auto& xs = P.T[O["input"].i32()].shape; auto& ws = P.T[O["weight"].i32()].shape;
+      c.B = (int)xs[0]; c.Cin = (int)xs[1]; c.H = (int)xs[2]; c.W = (int)xs[3];
+      c.Cout = (int)ws[0]; c.kH = (int)ws[2]; c.kW = (int)ws[3]; c.Hout = (int)os[2]; c.Wout = (int)os[3];
+    } else if (k == "conv2d_input_grad") {
+      auto& ws = P.T[O["weight"].i32()].shape; auto& ds = P.T[O["dy"].i32()].shape;
+      c.B = (int)os[0]; c.Cin = (int)os[1]; c.H = (int)os[2]; c.W = (int)os[3];
+      c.Cout = (int)ws[0]; c.kH = (int)ws[2]; c.kW = (int)ws[3]; c.Hout = (int)ds[2]; c.Wout = (int)ds[3];
+      which = 1;
+    } else {
+      auto& xs = P.T[O["input"].i32()].shape; auto& ds = P.T[O["dy"].i32()].shape;
+      c.B = (int)xs[0]; c.Cin = (int)xs[1]; c.H = (int)xs[2]; c.W = (int)xs[3];
+      c.Cout = (int)os[0]; c.kH = (int)os[2]; c.kW = (int)os[3]; c.Hout = (int)ds[2]; c.Wout = (int)ds[3];
+      which = 2;
+    }
+    return conv_gemm_scratch_floats(c, which) * 4;
+  }
   if (k == "sum_to_shape") {
     int a = P.op(i)["a"].i32();
     int64_t inner = P.T[P.out[i]].numel, outer = P.T[a].numel / std::max<int64_t>(inner, 1);
@@ -844,7 +868,8 @@ void Graph::emit_launches() {
         c.B = (int)xs[0]; c.Cin = (int)xs[1]; c.H = (int)xs[2]; c.W = (int)xs[3];
         c.Cout = (int)ws[0]; c.kH = (int)ws[2]; c.kW = (int)ws[3]; c.Hout = (int)os[2]; c.Wout = (int)os[3];
         const float* xp = (const float*)ptr(x); const float* wp = (const float*)ptr(w); float* yp = (float*)ptr(o);
-        add(k, [=](cudaStream_t s) { launch_conv2d(c, xp, wp, yp, s); });
+        float* sc = (float*)scratch; int64_t sf = (int64_t)scratch_floats;
+        add(k, [=](cudaStream_t s) { launch_conv2d_gemm(c, xp, wp, yp, sc, sf, s); });
       } else if (k == "conv2d_input_grad") {
         int w = O["weight"].i32(), dy = O["dy"].i32();
         ensure_contig(w, k.c_str()); ensure_contig(dy, k.c_str());
@@ -852,7 +877,8 @@ void Graph::emit_launches() {
         c.B = (int)os[0]; c.Cin = (int)os[1]; c.H = (int)os[2]; c.W = (int)os[3];
         c.Cout = (int)ws[0]; c.kH = (int)ws[2]; c.kW = (int)ws[3]; c.Hout = (int)ds[2]; c.Wout = (int)ds[3];
         const float* wp = (const float*)ptr(w); const float* dp2 = (const float*)ptr(dy); float* xp = (float*)ptr(o);
-        add(k, [=](cudaStream_t s) { launch_conv2d_input_grad(c, wp, dp2, xp, s); });
+        float* sc = (float*)scratch; int64_t sf = (int64_t)scratch_floats;
+        add(k, [=](cudaStream_t s) { launch_conv2d_input_grad_gemm(c, wp, dp2, xp, sc, sf, s); });
       } else if (k == "conv2d_weight_grad") {
         int x = O["input"].i32(), dy = O["dy"].i32();
         ensure_contig(x, k.c_str()); ensure_contig(dy, k.c_str());
@@ -860,7 +886,8 @@ void Graph::emit_launches() {
         c.B = (int)xs[0]; c.Cin = (int)xs[1]; c.H = (int)xs[2]; c.W = (int)xs[3];
         c.Cout = (int)os[0]; c.kH = (int)os[2]; c.kW = (int)os[3]; c.Hout = (int)ds[2]; c.Wout = (int)ds[3];
         const float* xp = (const float*)ptr(x); const float* dp2 = (const float*)ptr(dy); float* wp = (float*)ptr(o);
-        add(k, [=](cudaStream_t s) { launch_conv2d_weight_grad(c, xp, dp2, wp, s); });
+        float* sc = (float*)scratch; int64_t sf = (int64_t)scratch_floats;
+        add(k, [=](cudaStream_t s) { launch_conv2d_weight_grad_gemm(c, xp, dp2, wp, sc, sf, s); });
       } else {
         int x = O["input"].i32();
         ensure_contig(x, k.c_str());

@@ -193,6 +193,28 @@ def test_conv_and_pool(ctx):
     run(ctx, lambda: tg.maxPool2d(T("x", [2, 3, 8, 8]), 3, stride=2, padding=1), {"x": q}, exact=True)
 
 
+@pytest.mark.parametrize("B,Cin,H,W,Cout,k,stride,pad,groups", [
+    (8, 16, 20, 20, 32, 3, 1, 1, 1),   # every contraction on the tensor-core path
+    (4, 1, 28, 28, 8, 3, 1, 0, 1),     # Cin=1: K=9 forward on the SIMT path
+    (3, 6, 11, 9, 9, 3, 2, 1, 3),      # groups, stride 2, ragged spatial sizes
+    (2, 4, 7, 7, 4, 5, 1, 2, 2),       # 5x5 taps wider than the stride
+])
+def test_conv_forward_and_grads(ctx, B, Cin, H, W, Cout, k, stride, pad, groups):
+    """conv2d, conv2d_input_grad and conv2d_weight_grad through the column
+    gather + GEMM lowering against the oracle's direct sums."""
+    Ho = (H + 2 * pad - k) // stride + 1
+    Wo = (W + 2 * pad - k) // stride + 1
+    x = rnd([B, Cin, H, W], 40)
+    w = rnd([Cout, Cin // groups, k, k], 41)
+    dy = rnd([B, Cout, Ho, Wo], 42)
+    run(ctx, lambda: tg.conv2d(T("x", list(x.shape)), T("w", list(w.shape)), stride=stride, padding=pad,
+                               groups=groups), {"x": x, "w": w})
+    run(ctx, lambda: tg.conv2dInputGrad(T("w", list(w.shape)), T("dy", list(dy.shape)), H, W, stride, stride,
+                                        pad, pad, groups), {"w": w, "dy": dy})
+    run(ctx, lambda: tg.conv2dWeightGrad(T("x", list(x.shape)), T("dy", list(dy.shape)), k, k, stride, stride,
+                                         pad, pad, groups), {"x": x, "dy": dy})
+
+
 def test_randn_and_categorical(ctx):
     seed = np.array(5, np.int32)
     run(ctx, lambda: tg.add(tg.randn([4, 1000]), T("z", [1000])), {"z": np.zeros(1000, np.float32),
