@@ -3,6 +3,8 @@
 #include <cuda_runtime.h>
 #include <cstdint>
 #include <cstddef>
+#include <functional>
+#include <string>
 
 namespace tg {
 
@@ -102,6 +104,9 @@ int64_t colsum_chunks(int64_t outer, int64_t inner);
 void launch_colsum_fold(const float* part, float* out, int64_t nchunk, int64_t inner, cudaStream_t s);
 void launch_colsum(const float* x, float* out, int64_t outer, int64_t inner, float* scratch, cudaStream_t s);
 // General sum-to-shape: keep[d] = 1 where the output keeps input axis d.
+// out[c] = sum of x[b, c, i] over b < R1, i < R2 (deterministic two-pass).
+int64_t sum_mid_scratch_floats(int64_t R1, int64_t K);
+void launch_sum_mid(const float* x, float* out, int64_t R1, int64_t K, int64_t R2, float* scratch, cudaStream_t s);
 void launch_sum_general(const float* x, float* out, int rank, const int64_t* in_dims, const int64_t* keep,
                         int64_t in_numel, int64_t out_numel, cudaStream_t s);
 
@@ -170,14 +175,12 @@ struct ConvDesc {
   int B, Cin, H, W, Cout, kH, kW, Hout, Wout, sH, sW, pH, pW, G;
 };
 // conv2d and both gradients as column gathers plus GEMMs (kernels_conv.cu).
-// `which`: 0 forward, 1 input grad, 2 weight grad.
+// `which`: 0 forward (in0 = x, in1 = w, out = y), 1 input grad (w, dy, dx),
+// 2 weight grad (x, dy, dw). emit_conv hands each launch, labelled, to `add`.
+using ConvEmit = std::function<void(const std::string&, std::function<void(cudaStream_t)>)>;
 int64_t conv_gemm_scratch_floats(const ConvDesc& c, int which);
-void launch_conv2d_gemm(const ConvDesc& c, const float* x, const float* w, float* y, float* scratch,
-                        int64_t scratch_floats, cudaStream_t s);
-void launch_conv2d_input_grad_gemm(const ConvDesc& c, const float* w, const float* dy, float* dx, float* scratch,
-                                   int64_t scratch_floats, cudaStream_t s);
-void launch_conv2d_weight_grad_gemm(const ConvDesc& c, const float* x, const float* dy, float* dw, float* scratch,
-                                    int64_t scratch_floats, cudaStream_t s);
+void emit_conv(int which, const ConvDesc& c, const float* in0, const float* in1, float* out, float* scratch,
+               int64_t scratch_floats, const ConvEmit& add);
 void launch_maxpool(const ConvDesc& c, const float* x, float* y, cudaStream_t s);
 void launch_maxpool_grad(const ConvDesc& c, const float* x, const float* dy, float* dx, cudaStream_t s);
 

@@ -333,8 +333,78 @@ __global__ void maxpool_grad_kernel(const __grid_constant__ ConvDesc c, const fl
     dx[i] = s;
   }
 }
+// Windows that do not overlap (stride >= window on both axes): each input
+// element lies in at most one window, found directly; 32-bit indexing. The
+// window's first maximum is recomputed with the forward's scan order.
+__global__ void __launch_bounds__(256) maxpool_grad_disjoint_kernel(const __grid_constant__ ConvDesc c,
+                                                                    const float* __restrict__ x,
+                                                                    const float* __restrict__ dy,
+                                                                    float* __restrict__ dx) {
+  const int total = c.B * c.Cin * c.H * c.W;
+  const int hw = c.H * c.W;
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < total; i += gridDim.x * blockDim.x) {
+    const int bc = i / hw, r = i - bc * hw;
+    const int hi = r / c.W, wi = r - hi * c.W;
+    const int nh = hi + c.pH, nw = wi + c.pW;
+    const int ho = nh / c.sH, wo = nw / c.sW;
+    float v = 0.f;
+    if (nh - ho * c.sH < c.kH && nw - wo * c.sW < c.kW && ho < c.Hout && wo < c.Wout) {
+      const float* xb = x + (int64_t)bc * hw;
+      float m = -3.4e38f;
+      int ah = -1, aw = -1;
+      for (int a = 0; a < c.kH; ++a) {
+        const int hh = ho * c.sH + a - c.pH;
+        if (hh < 0 || hh >= c.H) continue;
+        for (int b2 = 0; b2 < c.kW; ++b2) {
+          const int ww = wo * c.sW + b2 - c.pW;
+          if (ww < 0 || ww >= c.W) continue;
+          const float xv = xb[hh * c.W + ww];
+          if (xv > m) { m = xv; ah = hh; aw = ww; }
+        }
+      }
+      if (ah == hi && aw == wi) v = dy[(int64_t)bc * c.Hout * c.Wout + ho * c.Wout + wo];
+    }
+    dx[i] = v;
+  }
+}
+
+// 2x2 windows, stride 2, no padding, tiling the input exactly: one thread
+// per window reads its four inputs (two float2 loads), picks the first
+// maximum in the forward's scan order (from -3.4e38 with strict '>', so a
+// window with no element above that routes no gradient) and writes dy there
+// and 0 elsewhere.
+__global__ void __launch_bounds__(256) maxpool2_grad_kernel(int planes, int Hout, int Wout,
+                                                            const float* __restrict__ x,
+                                                            const float* __restrict__ dy, float* __restrict__ dx) {
+  const int total = planes * Hout * Wout, W = 2 * Wout;
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < total; i += gridDim.x * blockDim.x) {
+    const int pl = i / (Hout * Wout), r = i - pl * (Hout * Wout);
+    const int ho = r / Wout, wo = r - ho * Wout;
+    const int64_t top = (int64_t)pl * (4 * Hout * Wout) + (2 * ho) * W + 2 * wo;
+    const float2 a = *reinterpret_cast<const float2*>(x + top);
+    const float2 b = *reinterpret_cast<const float2*>(x + top + W);
+    float m = -3.4e38f;
+    int at = -1;
+    if (a.x > m) { m = a.x; at = 0; }
+    if (a.y > m) { m = a.y; at = 1; }
+    if (b.x > m) { m = b.x; at = 2; }
+    if (b.y > m) { m = b.y; at = 3; }
+    const float g = dy[i];
+    *reinterpret_cast<float2*>(dx + top) = make_float2(at == 0 ? g : 0.f, at == 1 ? g : 0.f);
+    *reinterpret_cast<float2*>(dx + top + W) = make_float2(at == 2 ? g : 0.f, at == 3 ? g : 0.f);
+  }
+}
+
 void launch_maxpool_grad(const ConvDesc& c, const float* x, const float* dy, float* dx, cudaStream_t s) {
-  maxpool_grad_kernel<<<grid_for((int64_t)c.B * c.Cin * c.H * c.W), 256, 0, s>>>(c, x, dy, dx);
+  const int64_t total = (int64_t)c.B * c.Cin * c.H * c.W;
+  if (c.kH == 2 && c.kW == 2 && c.sH == 2 && c.sW == 2 && c.pH == 0 && c.pW == 0 && c.H == 2 * c.Hout &&
+      c.W == 2 * c.Wout && total < INT32_MAX && !(reinterpret_cast<uintptr_t>(x) & 7) &&
+      !(reinterpret_cast<uintptr_t>(dx) & 7))
+    maxpool2_grad_kernel<<<grid_for(total / 4, 256, 16), 256, 0, s>>>(c.B * c.Cin, c.Hout, c.Wout, x, dy, dx);
+  else if (c.sH >= c.kH && c.sW >= c.kW && total < INT32_MAX)
+    maxpool_grad_disjoint_kernel<<<grid_for(total, 256, 16), 256, 0, s>>>(c, x, dy, dx);
+  else
+    maxpool_grad_kernel<<<grid_for(total), 256, 0, s>>>(c, x, dy, dx);
 }
 
 // ------------------------------------------------------------ optimizers --

@@ -448,6 +448,50 @@ __global__ void __launch_bounds__(256) sum_general_kernel(const float* __restric
   }
 }
 
+// ------------------------------------------------ middle-axis sum [R1,K,R2] --
+// out[c] = sum over b < R1, i < R2 of x[(b*K + c)*R2 + i] (a conv bias
+// gradient: batch and spatial axes reduced, channels kept). Block (c, s) sums
+// the batch slice s of channel c reading contiguous R2-runs; partials
+// part[s*K + c] are then folded over s in order, so the result does not
+// depend on scheduling.
+static int64_t sum_mid_slices(int64_t R1, int64_t K) {
+  int64_t s = (4 * (int64_t)device_sm_count() + K - 1) / K;
+  if (s > R1) s = R1;
+  if (s > 64) s = 64;
+  return s < 1 ? 1 : s;
+}
+
+int64_t sum_mid_scratch_floats(int64_t R1, int64_t K) { return sum_mid_slices(R1, K) * K; }
+
+__global__ void __launch_bounds__(256) sum_mid_partial_kernel(const float* __restrict__ x, float* __restrict__ part,
+                                                              int64_t R1, int64_t K, int64_t R2, int64_t per) {
+  __shared__ float sm[8];
+  const int64_t c = blockIdx.x, sl = blockIdx.y;
+  const int64_t b0 = sl * per, b1 = b0 + per < R1 ? b0 + per : R1;
+  float acc = 0.f;
+  for (int64_t b = b0; b < b1; ++b) {
+    const float* row = x + (b * K + c) * R2;
+    for (int64_t i = threadIdx.x; i < R2; i += blockDim.x) acc += row[i];
+  }
+  acc = warp_sum(acc);
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+  if (lane == 0) sm[wid] = acc;
+  __syncthreads();
+  if (wid == 0) {
+    acc = lane < 8 ? sm[lane] : 0.f;
+    acc = warp_sum(acc);
+    if (lane == 0) part[sl * K + c] = acc;
+  }
+}
+
+void launch_sum_mid(const float* x, float* out, int64_t R1, int64_t K, int64_t R2, float* scratch, cudaStream_t s) {
+  const int64_t S = sum_mid_slices(R1, K);
+  const int64_t per = (R1 + S - 1) / S;
+  const int64_t used = (R1 + per - 1) / per;
+  sum_mid_partial_kernel<<<dim3((unsigned)K, (unsigned)used), 256, 0, s>>>(x, scratch, R1, K, R2, per);
+  launch_colsum_fold(scratch, out, used, K, s);
+}
+
 void launch_sum_general(const float* x, float* out, int rank, const int64_t* in_dims, const int64_t* keep,
                         int64_t in_numel, int64_t out_numel, cudaStream_t s) {
   SumGen g{};

@@ -112,6 +112,26 @@ int64_t Graph::param_numel(const std::string& name) const {
 }
 
 // Scratch bytes an op's launch needs (shared buffer: launches are serial).
+// Whether the kept dims of a reduction form one contiguous run with reduced
+// dims on both sides ([R1, K, R2] after merging); fills the three extents.
+static bool mid_runs(const std::vector<int64_t>& is, const std::vector<int64_t>& keep, int64_t* r3) {
+  int64_t e[3] = {1, 1, 1};
+  int phase = 0;  // 0: leading reduced, 1: kept, 2: trailing reduced
+  for (size_t d = 0; d < is.size(); ++d) {
+    if (is[d] == 1) continue;
+    if (keep[d]) {
+      if (phase == 2) return false;
+      phase = 1;
+    } else if (phase == 1) {
+      phase = 2;
+    }
+    e[phase] *= is[d];
+  }
+  if (phase != 2 || e[0] == 1) return false;
+  if (r3) { r3[0] = e[0]; r3[1] = e[1]; r3[2] = e[2]; }
+  return true;
+}
+
 static int64_t scratch_for(const Program& P, int i, int action) {
   const std::string& k = P.kind[i];
   if (action == 101) {
@@ -161,7 +181,8 @@ static int64_t scratch_for(const Program& P, int i, int action) {
   if (k == "sum_to_shape") {
     int a = P.op(i)["a"].i32();
     int64_t inner = P.T[P.out[i]].numel, outer = P.T[a].numel / std::max<int64_t>(inner, 1);
-    return (int64_t)std::max(colsum_scratch_floats(outer, inner), row_scratch_floats(ROW_SUM, inner, outer)) * 4;
+    int64_t f = std::max<int64_t>(colsum_scratch_floats(outer, inner), row_scratch_floats(ROW_SUM, inner, outer));
+    return std::max<int64_t>(f, sum_mid_scratch_floats(outer, inner)) * 4;
   }
   return 0;
 }
@@ -720,6 +741,11 @@ void Graph::emit_launches() {
       int64_t inner = P.T[o].numel, outer = P.T[a].numel / std::max<int64_t>(inner, 1);
       if (suffix) {
         add("colsum", [=](cudaStream_t s) { launch_colsum(x, out, outer, inner, scratch, s); });
+      } else if (mid_runs(is, keep, nullptr)) {
+        int64_t r3[3];
+        mid_runs(is, keep, r3);
+        const int64_t R1 = r3[0], Km = r3[1], R2 = r3[2];
+        add("sum_mid", [=](cudaStream_t s) { launch_sum_mid(x, out, R1, Km, R2, scratch, s); });
       } else {
         std::vector<int64_t> dims = is;
         int64_t in_n = P.T[a].numel, out_n = inner;
@@ -869,7 +895,7 @@ void Graph::emit_launches() {
         c.Cout = (int)ws[0]; c.kH = (int)ws[2]; c.kW = (int)ws[3]; c.Hout = (int)os[2]; c.Wout = (int)os[3];
         const float* xp = (const float*)ptr(x); const float* wp = (const float*)ptr(w); float* yp = (float*)ptr(o);
         float* sc = (float*)scratch; int64_t sf = (int64_t)scratch_floats;
-        add(k, [=](cudaStream_t s) { launch_conv2d_gemm(c, xp, wp, yp, sc, sf, s); });
+        emit_conv(0, c, xp, wp, yp, sc, sf, add);
       } else if (k == "conv2d_input_grad") {
         int w = O["weight"].i32(), dy = O["dy"].i32();
         ensure_contig(w, k.c_str()); ensure_contig(dy, k.c_str());
@@ -878,7 +904,7 @@ void Graph::emit_launches() {
         c.Cout = (int)ws[0]; c.kH = (int)ws[2]; c.kW = (int)ws[3]; c.Hout = (int)ds[2]; c.Wout = (int)ds[3];
         const float* wp = (const float*)ptr(w); const float* dp2 = (const float*)ptr(dy); float* xp = (float*)ptr(o);
         float* sc = (float*)scratch; int64_t sf = (int64_t)scratch_floats;
-        add(k, [=](cudaStream_t s) { launch_conv2d_input_grad_gemm(c, wp, dp2, xp, sc, sf, s); });
+        emit_conv(1, c, wp, dp2, xp, sc, sf, add);
       } else if (k == "conv2d_weight_grad") {
         int x = O["input"].i32(), dy = O["dy"].i32();
         ensure_contig(x, k.c_str()); ensure_contig(dy, k.c_str());
@@ -887,7 +913,7 @@ void Graph::emit_launches() {
         c.Cout = (int)os[0]; c.kH = (int)os[2]; c.kW = (int)os[3]; c.Hout = (int)ds[2]; c.Wout = (int)ds[3];
         const float* xp = (const float*)ptr(x); const float* dp2 = (const float*)ptr(dy); float* wp = (float*)ptr(o);
         float* sc = (float*)scratch; int64_t sf = (int64_t)scratch_floats;
-        add(k, [=](cudaStream_t s) { launch_conv2d_weight_grad_gemm(c, xp, dp2, wp, sc, sf, s); });
+        emit_conv(2, c, xp, dp2, wp, sc, sf, add);
       } else {
         int x = O["input"].i32();
         ensure_contig(x, k.c_str());

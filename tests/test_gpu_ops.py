@@ -156,6 +156,15 @@ def test_sum_to_shape_trailing(ctx):
     run(ctx, lambda: tg.sumToShape(T("b", [3, 40000]), [3, 1]), {"b": b})
 
 
+def test_sum_to_shape_middle(ctx):
+    """Reduced dims on both sides of the kept ones (the conv bias gradient
+    [B, C, H, W] -> [C, 1, 1]), small and at the CNN benchmark's size."""
+    a = rnd([3, 5, 4, 7], 63)
+    run(ctx, lambda: tg.sumToShape(T("a", [3, 5, 4, 7]), [5, 1, 1]), {"a": a})
+    b = rnd([128, 64, 24, 24], 64)
+    run(ctx, lambda: tg.sumToShape(T("b", [128, 64, 24, 24]), [64, 1, 1]), {"b": b})
+
+
 @pytest.mark.parametrize("M,K,N", [(1, 1, 1), (37, 29, 53), (256, 384, 200), (130, 1, 70)])
 def test_matmul_2d(ctx, M, K, N):
     run(ctx, lambda: tg.matmul(T("a", [M, K]), T("b", [K, N])), {"a": rnd([M, K], 21), "b": rnd([K, N], 22)})
@@ -191,6 +200,20 @@ def test_conv_and_pool(ctx):
     q = np.floor(rnd([2, 3, 8, 8], 32, 0, 3)).astype(np.float32)
     run(ctx, lambda: tg.maxPool2d(T("x", [2, 3, 8, 8]), 2), {"x": q}, exact=True)
     run(ctx, lambda: tg.maxPool2d(T("x", [2, 3, 8, 8]), 3, stride=2, padding=1), {"x": q}, exact=True)
+
+
+@pytest.mark.parametrize("shape,k,stride,pad", [([3, 4, 8, 6], 2, 2, 0), ([2, 3, 9, 7], 2, 2, 0),
+                                                 ([2, 3, 9, 9], 3, 3, 1), ([2, 2, 8, 8], 3, 2, 1)])
+def test_maxpool_grad(ctx, shape, k, stride, pad):
+    """Max-pool gradient on exact 2x2 tilings, ragged edges, padded disjoint
+    windows and overlapping windows; ties (integer-valued inputs) must route
+    to the first maximum in scan order, bit for bit."""
+    q = np.floor(rnd(shape, 34, 0, 3)).astype(np.float32)
+    Ho = (shape[2] + 2 * pad - k) // stride + 1
+    Wo = (shape[3] + 2 * pad - k) // stride + 1
+    dy = rnd([shape[0], shape[1], Ho, Wo], 35)
+    run(ctx, lambda: tg.maxPool2dGrad(T("x", shape), T("dy", list(dy.shape)), k, k, stride, stride, pad, pad),
+        {"x": q, "dy": dy}, exact=True)
 
 
 @pytest.mark.parametrize("B,Cin,H,W,Cout,k,stride,pad,groups", [
