@@ -101,6 +101,7 @@ size_t colsum_scratch_floats(int64_t outer, int64_t inner);
 // Chunking of the two-pass column sum (chunks of consecutive rows) and its
 // second pass, shared with generated kernels that compute the first pass.
 int64_t colsum_chunks(int64_t outer, int64_t inner);
+int64_t colsum_col_blocks(int64_t inner, bool vec);
 void launch_colsum_fold(const float* part, float* out, int64_t nchunk, int64_t inner, cudaStream_t s);
 void launch_colsum(const float* x, float* out, int64_t outer, int64_t inner, float* scratch, cudaStream_t s);
 // General sum-to-shape: keep[d] = 1 where the output keeps input axis d.

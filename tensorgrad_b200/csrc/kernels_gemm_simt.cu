@@ -71,7 +71,7 @@ __global__ void __launch_bounds__(256) sgemm_kernel(const __grid_constant__ Gemm
         g.workspace[((sp * g.batch + bz) * g.M + gm) * g.N + gn] = acc[i][j];
         continue;
       }
-      float v = acc[i][j] * g.alpha;
+      float v = __fmul_rn(acc[i][j], g.alpha);
       if (g.bias) v += g.bias[gn];
       float* c = C + gm * g.ldc + gn * (g.ldc_n ? g.ldc_n : 1);
       *c = g.accumulate ? *c + v : v;
@@ -86,7 +86,7 @@ __global__ void __launch_bounds__(256) sgemm_splitk_reduce(const __grid_constant
     const int64_t bz = e / per, rem = e % per, m = rem / g.N, n = rem % g.N;
     float v = 0.f;
     for (int sp = 0; sp < splits; ++sp) v += g.workspace[sp * total + e];
-    v *= g.alpha;
+    v = __fmul_rn(v, g.alpha);
     if (g.bias) v += g.bias[n];
     const int64_t i1 = bz / g.batch2, i2 = bz % g.batch2;
     float* c = g.C + i1 * g.c_batch + i2 * g.c_batch2 + m * g.ldc + n * (g.ldc_n ? g.ldc_n : 1);

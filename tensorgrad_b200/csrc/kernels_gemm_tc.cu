@@ -534,7 +534,7 @@ __global__ void __launch_bounds__(448, 1) gemm_tc_kernel(const __grid_constant__
 #pragma unroll
                   for (int q = 0; q < 4; ++q) {
                     const int jc = 32 * jj + 4 * c + q;
-                    v[q] = sum[jc] * alpha + brow;
+                    v[q] = __fmul_rn(sum[jc], alpha) + brow;  // alpha rounds alone, as a separate scale would
                     if (bias && !bias_m && U.n0 + cb + jc < P.N) v[q] += bias[U.n0 + cb + jc];
                   }
                   *reinterpret_cast<float4*>(sub + r * 128 + ((c ^ (r & 7)) << 4)) = make_float4(v[0], v[1], v[2], v[3]);
@@ -547,7 +547,7 @@ __global__ void __launch_bounds__(448, 1) gemm_tc_kernel(const __grid_constant__
 #pragma unroll
               for (int j = 0; j < 64; ++j) {
                 const int n = cb + j;
-                float v = sum[j] * alpha + brow;
+                float v = __fmul_rn(sum[j], alpha) + brow;
                 if (bias && !bias_m && U.n0 + n < P.N) v += bias[U.n0 + n];
                 *reinterpret_cast<float*>(sub + n * 128 + ((mc ^ (n & 7)) << 4)) = v;
               }
@@ -576,7 +576,7 @@ __global__ void __launch_bounds__(448, 1) gemm_tc_kernel(const __grid_constant__
           for (int j = 0; j < 64; ++j) {
             const int64_t col = U.n0 + cb + j;
             if (col < P.N) {
-              float v = sum[j] * alpha;
+              float v = __fmul_rn(sum[j], alpha);
               if (bias) v += bias[bias_m ? row : col];
               float* d = C + row * cm + col * cn;
               *d = accumulate ? *d + v : v;
@@ -609,7 +609,7 @@ __global__ void __launch_bounds__(256) gemm_splitk_reduce(const __grid_constant_
     const int64_t w = zb * per + row * P.N + col;
     float v = 0.f;
     for (int sp = 0; sp < P.splits; ++sp) v += P.ws[(int64_t)sp * total + w];
-    v *= P.alpha;
+    v = __fmul_rn(v, P.alpha);
     if (P.bias) v += P.bias[P.bias_m ? row : col];
     const int64_t i1 = zb / P.batch2, i2 = zb % P.batch2;
     float* d = P.C + i1 * P.c_batch + i2 * P.c_batch2 + row * P.c_m + col * P.c_n;

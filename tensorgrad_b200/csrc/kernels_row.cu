@@ -325,12 +325,24 @@ void launch_row(int kind, const float* x, void* out, int64_t rows, int64_t D, cu
 }
 
 // -------------------------------------------------------------- column sum --
+// Column sums run in 256-thread blocks of 32 column threads (one column, or
+// four adjacent columns in the float4 form) x 8 row groups: row group g of
+// chunk c sums rows r0+g, r0+g+8, ... ascending; the 8 group sums are added
+// in group order through shared memory; chunk partials are folded in chunk
+// order. The fused column reductions use the same blocks and chunks, so every
+// column is summed in the same order whichever kernel runs.
+int64_t colsum_col_blocks(int64_t inner, bool vec) {
+  const int64_t cols = vec ? (inner + 3) / 4 : inner;
+  return (cols + 31) / 32;
+}
+
+// Row chunks: about four blocks per SM, at least 64 rows per chunk.
 int64_t colsum_chunks(int64_t outer, int64_t inner) {
-  int sms = device_sm_count();
-  int64_t colblocks = (inner + 255) / 256;
-  int64_t want = ((int64_t)sms * 4 + colblocks - 1) / colblocks;
-  int64_t maxc = (outer + 63) / 64;  // at least 64 rows per chunk
-  int64_t c = want < maxc ? want : maxc;
+  const int64_t sms = device_sm_count();
+  const int64_t cb = colsum_col_blocks(inner, inner % 4 == 0);
+  const int64_t want = (4 * sms + cb - 1) / cb;
+  const int64_t maxc = (outer + 63) / 64;
+  const int64_t c = want < maxc ? want : maxc;
   return c < 1 ? 1 : c;
 }
 
@@ -339,24 +351,41 @@ size_t colsum_scratch_floats(int64_t outer, int64_t inner) {
   return c > 1 ? (size_t)(c * inner) : 0;
 }
 
+template <bool VEC>
 __global__ void __launch_bounds__(256) colsum_partial_kernel(const float* __restrict__ x, float* __restrict__ part,
                                                              int64_t outer, int64_t inner, int64_t rows_per) {
-  int64_t col = (int64_t)blockIdx.x * 256 + threadIdx.x;
-  int64_t c = blockIdx.y;
-  if (col >= inner) return;
-  int64_t r0 = c * rows_per, r1 = r0 + rows_per < outer ? r0 + rows_per : outer;
-  // rows in ascending order; 8 independent loads in flight per thread
-  float s = 0.f;
-  int64_t r = r0;
-  for (; r + 8 <= r1; r += 8) {
-    float v[8];
+  constexpr int W = VEC ? 4 : 1;
+  __shared__ float red[8][32 * W];
+  const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;
+  const int64_t col = ((int64_t)blockIdx.x * 32 + tx) * W;
+  const int64_t c = blockIdx.y;
+  const int64_t r0 = c * rows_per, r1 = r0 + rows_per < outer ? r0 + rows_per : outer;
+  float acc[W];
 #pragma unroll
-    for (int u = 0; u < 8; ++u) v[u] = __ldg(x + (r + u) * inner + col);
-#pragma unroll
-    for (int u = 0; u < 8; ++u) s += v[u];
+  for (int l = 0; l < W; ++l) acc[l] = 0.f;
+  if (col < inner) {
+#pragma unroll 4
+    for (int64_t r = r0 + ty; r < r1; r += 8) {
+      if constexpr (VEC) {
+        const float4 v = __ldg(reinterpret_cast<const float4*>(x + r * inner + col));
+        acc[0] += v.x; acc[1] += v.y; acc[2] += v.z; acc[3] += v.w;
+      } else {
+        acc[0] += __ldg(x + r * inner + col);
+      }
+    }
   }
-  for (; r < r1; ++r) s += __ldg(x + r * inner + col);
-  part[c * inner + col] = s;
+#pragma unroll
+  for (int l = 0; l < W; ++l) red[ty][tx * W + l] = acc[l];
+  __syncthreads();
+  if (ty == 0 && col < inner) {
+#pragma unroll
+    for (int l = 0; l < W; ++l) {
+      float t = 0.f;
+#pragma unroll
+      for (int g = 0; g < 8; ++g) t += red[g][tx * W + l];
+      part[c * inner + col + l] = t;
+    }
+  }
 }
 
 // 32 columns per block; warp w sums chunks w, w+8, ... (coalesced across the
@@ -393,15 +422,18 @@ void launch_colsum_fold(const float* part, float* out, int64_t nchunk, int64_t i
 
 void launch_colsum(const float* x, float* out, int64_t outer, int64_t inner, float* scratch, cudaStream_t s) {
   if (inner <= 0) return;
-  int64_t c = colsum_chunks(outer, inner);
-  unsigned gx = (unsigned)((inner + 255) / 256);
-  if (c <= 1 || !scratch) {
-    colsum_partial_kernel<<<dim3(gx, 1), 256, 0, s>>>(x, out, outer, inner, outer);
-    return;
-  }
-  int64_t rows_per = (outer + c - 1) / c;
-  colsum_partial_kernel<<<dim3(gx, (unsigned)c), 256, 0, s>>>(x, scratch, outer, inner, rows_per);
-  colsum_fold_kernel<<<(unsigned)((inner + 31) / 32), 256, 0, s>>>(scratch, out, c, inner);
+  const int64_t c = colsum_chunks(outer, inner);
+  const bool chunked = c > 1 && scratch;
+  float* dst = chunked ? scratch : out;
+  const bool vec = inner % 4 == 0 && !(reinterpret_cast<uintptr_t>(x) & 15);
+  const unsigned gx = (unsigned)colsum_col_blocks(inner, vec);
+  const int64_t nc = chunked ? c : 1;
+  const int64_t rows_per = (outer + nc - 1) / nc;
+  if (vec)
+    colsum_partial_kernel<true><<<dim3(gx, (unsigned)nc), 256, 0, s>>>(x, dst, outer, inner, rows_per);
+  else
+    colsum_partial_kernel<false><<<dim3(gx, (unsigned)nc), 256, 0, s>>>(x, dst, outer, inner, rows_per);
+  if (chunked) launch_colsum_fold(scratch, out, nc, inner, s);
 }
 
 // ---------------------------------------------------- general sum to shape --

@@ -181,6 +181,7 @@ class Graph {
   std::vector<int> action_;          // per op: planned action code
   std::vector<StorageLoc> loc_;      // per root tensor
   std::vector<int> op_done_;         // ops folded away
+  std::vector<float> gemm_alpha_;    // per GEMM op: output scale folded in from a following mul_scalar
   // Fused elementwise groups. A group is rooted at the op whose output it
   // writes: its last elementwise member, or a reduction that consumes it.
   struct EwGroup {

@@ -73,6 +73,7 @@ Graph::~Graph() {
 void Graph::plan() {
   action_.assign(P.ops.size(), 0);
   op_done_.assign(P.ops.size(), 0);
+  gemm_alpha_.assign(P.ops.size(), 1.f);
   for (size_t i = 0; i < P.ops.size(); ++i) {
     if (is_leaf_kind(P.kind[i]) || is_const_kind(P.kind[i])) op_done_[i] = 1;
   }
@@ -767,7 +768,7 @@ void Graph::emit_launches() {
       GemmDesc g{};
       g.K = as[ra - 1];
       g.N = bs[rb - 1];
-      g.alpha = 1.f;
+      g.alpha = gemm_alpha_[i];
       g.A = reinterpret_cast<const float*>(ptr(a));
       g.B = reinterpret_cast<const float*>(ptr(b));
       g.C = reinterpret_cast<float*>(ptr(o));

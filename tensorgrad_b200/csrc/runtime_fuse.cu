@@ -340,7 +340,9 @@ void Graph::emit_ew_group(int gi, const int* seed_ptr, float* scratch, size_t sc
   int64_t rows = 0, len = 0;
   const RedShape rs = G.red >= 0 ? red_shape(P, G.red, &rows, &len) : RED_NONE;
   if (G.red >= 0 && rs == RED_NONE) throw TgError("Error", "internal: fused reduction of an unsupported shape");
-  bool vec = rs == RED_NONE;
+  // float4 form: plain elementwise groups, and column sums over rows whose
+  // length is a multiple of 4 (four adjacent columns per thread)
+  bool vec = rs == RED_NONE || (rs == RED_COL && len % 4 == 0);
   std::vector<EwInput> ins;
   std::map<int, int> slot_of;
   bool has_drop = false;
@@ -369,6 +371,7 @@ void Graph::emit_ew_group(int gi, const int* seed_ptr, float* scratch, size_t sc
   const std::string value = "v" + std::to_string(vt);
   void* out = ptr(P.out[G.root]);
   if (rs == RED_NONE) vec = vec && n % 4 == 0 && ((uintptr_t)out & 15) == 0;
+  const int64_t col_chunks = rs == RED_COL ? colsum_chunks(rows, len) : 1;
   const int R = (int)os.size();
 
   // Per-element values of each input: for the vector form, loads before the
@@ -436,16 +439,33 @@ void Graph::emit_ew_group(int gi, const int* seed_ptr, float* scratch, size_t sc
   } else if (rs == RED_COL) {
     // first pass of the deterministic column sum: rows of chunk blockIdx.y in
     // ascending order (the unfused kernel's order); the fold is shared
-    nchunk = colsum_chunks(rows, len);
+    nchunk = col_chunks;
     if (nchunk > 1 && (!scratch || scratch_floats < (size_t)(nchunk * len)))
       throw TgError("Error", "internal: scratch too small for a fused column sum");
     const int64_t rp = (rows + nchunk - 1) / nchunk;
-    k << "  const i64 col = (i64)blockIdx.x * 256 + threadIdx.x;\n  if (col >= " << L << ") return;\n";
+    // 32 column threads (4 adjacent columns each in the float4 form) x 8 row
+    // groups, combined in group order: the unfused column sum's order
+    const int W = vec ? 4 : 1;
+    k << "  const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;\n";
+    k << "  __shared__ float red[8][" << 32 * W << "];\n";
+    k << "  const i64 col = ((i64)blockIdx.x * 32 + tx) * " << W << ";\n";
     k << "  const i64 r0 = (i64)blockIdx.y * " << rp << "ll;\n";
     k << "  const i64 r1 = r0 + " << rp << "ll < " << rows << "ll ? r0 + " << rp << "ll : " << rows << "ll;\n";
-    k << "  float acc = 0.f;\n#pragma unroll 4\n  for (i64 r = r0; r < r1; ++r) {\n      const i64 e = r * " << L << " + col;\n";
-    k << lane.str() << ops.str() << "      acc += " << value << ";\n  }\n";
-    k << "  out[(i64)blockIdx.y * " << L << " + col] = acc;\n}\n";
+    k << "  float acc[" << W << "];\n  for (int l = 0; l < " << W << "; ++l) acc[l] = 0.f;\n";
+    k << "  if (col < " << L << ") {\n#pragma unroll 2\n    for (i64 r = r0 + ty; r < r1; r += 8) {\n";
+    if (vec) {
+      k << "    const i64 i = r * " << L << " + col;\n" << pre.str();
+      k << "#pragma unroll\n    for (int l = 0; l < 4; ++l) {\n      const i64 e = i + l;\n";
+      k << lane.str() << ops.str() << "      acc[l] += " << value << ";\n    }\n";
+    } else {
+      k << "      const i64 e = r * " << L << " + col;\n";
+      k << lane.str() << ops.str() << "      acc[0] += " << value << ";\n";
+    }
+    k << "    }\n  }\n";
+    k << "  for (int l = 0; l < " << W << "; ++l) red[ty][tx * " << W << " + l] = acc[l];\n  __syncthreads();\n";
+    k << "  if (ty == 0 && col < " << L << ") {\n    for (int l = 0; l < " << W << "; ++l) {\n";
+    k << "      float t = 0.f;\n#pragma unroll\n      for (int g = 0; g < 8; ++g) t += red[g][tx * " << W << " + l];\n";
+    k << "      out[(i64)blockIdx.y * " << L << " + col + l] = t;\n    }\n  }\n}\n";
   } else if (vec) {
     k << "  for (i64 t = (i64)blockIdx.x * 256 + threadIdx.x; t < " << n / 4 << "ll; t += (i64)gridDim.x * 256) {\n";
     k << "    const i64 i = t * 4;\n" << pre.str();
@@ -482,11 +502,12 @@ void Graph::emit_ew_group(int gi, const int* seed_ptr, float* scratch, size_t sc
   A->drop_off = (long long)ctx->rank * n;
   const int64_t sms = device_sm_count();
   unsigned gx = 1, gy = 1;
+  int tpb = 256;
   if (rs == RED_ROW) {
     const int64_t blocks = (rows + 7) / 8;
     gx = (unsigned)std::max<int64_t>(1, std::min(blocks, sms * 16));
   } else if (rs == RED_COL) {
-    gx = (unsigned)((len + 255) / 256);
+    gx = (unsigned)colsum_col_blocks(len, vec);
     gy = (unsigned)nchunk;
   } else {
     const int64_t work = vec ? n / 4 : n;
@@ -498,13 +519,13 @@ void Graph::emit_ew_group(int gi, const int* seed_ptr, float* scratch, size_t sc
   float* fold_out = reinterpret_cast<float*>(out);
   const int64_t fold_n = (rs == RED_COL && nchunk > 1) ? nchunk : 0, fold_len = len;
   float* fold_part = scratch;
-  add(label, [fn, A, gx, gy, fold_n, fold_len, fold_part, fold_out](cudaStream_t s) {
+  add(label, [fn, A, gx, gy, tpb, fold_n, fold_len, fold_part, fold_out](cudaStream_t s) {
     std::vector<void*> args;
     for (auto& p : A->in) args.push_back(const_cast<const void**>(&p));
     args.push_back(&A->out);
     args.push_back(const_cast<const int**>(&A->seed));
     args.push_back(&A->drop_off);
-    jit_launch(*fn, gx, gy, 256, args.data(), s);
+    jit_launch(*fn, gx, gy, tpb, args.data(), s);
     if (fold_n > 0) launch_colsum_fold(fold_part, fold_out, fold_n, fold_len, s);
   });
 }

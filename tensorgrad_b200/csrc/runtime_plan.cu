@@ -254,6 +254,24 @@ void Graph::plan_views() {
     views_[a] = nv;
     op_done_[i] = 1;
   }
+
+  // A scale whose input only a GEMM writes and nothing else reads becomes
+  // that GEMM's alpha: the GEMM stores alpha * acc, rounded once as the
+  // mul_scalar would, straight into the scaled tensor's storage (attention's
+  // 1/sqrt(d) on the scores).
+  for (int i = 0; i < nO; ++i) {
+    if (op_done_[i] || P.kind[i] != "mul_scalar") continue;
+    int a = P.op(i)["a"].i32(), o = P.out[i];
+    int p = P.producer[a];
+    if (p < 0 || !is_gemm(p) || op_done_[p] || action_[p] != 0 || gemm_alpha_[p] != 1.f) continue;
+    if (observable.count(a) || P.consumers[a].size() != 1 || P.T[a].shape != P.T[o].shape) continue;
+    const TView& va = views_[a];
+    const TView& vo = views_[o];
+    if (va.root != a || !va.contiguous || va.onehot || vo.onehot || !vo.contiguous) continue;
+    views_[a] = vo;
+    gemm_alpha_[p] = (float)P.op(i)["scalar"].num();
+    op_done_[i] = 1;
+  }
 }
 
 // ------------------------------------------------------------ optimizer ----

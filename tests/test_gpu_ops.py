@@ -165,6 +165,15 @@ def test_sum_to_shape_middle(ctx):
     run(ctx, lambda: tg.sumToShape(T("b", [128, 64, 24, 24]), [64, 1, 1]), {"b": b})
 
 
+def test_scaled_gemm(ctx):
+    """mul_scalar folded into the producing GEMM's alpha (tensor-core and
+    SIMT paths, batched scores shape)."""
+    q, kt = rnd([4, 128, 64], 70), rnd([4, 64, 128], 71)
+    run(ctx, lambda: tg.mulScalar(tg.matmul(T("q", [4, 128, 64]), T("k", [4, 64, 128])), 0.125), {"q": q, "k": kt})
+    a, b = rnd([7, 5], 72), rnd([5, 9], 73)
+    run(ctx, lambda: tg.mulScalar(tg.matmul(T("a", [7, 5]), T("b", [5, 9])), -3.0), {"a": a, "b": b})
+
+
 @pytest.mark.parametrize("M,K,N", [(1, 1, 1), (37, 29, 53), (256, 384, 200), (130, 1, 70)])
 def test_matmul_2d(ctx, M, K, N):
     run(ctx, lambda: tg.matmul(T("a", [M, K]), T("b", [K, N])), {"a": rnd([M, K], 21), "b": rnd([K, N], 22)})

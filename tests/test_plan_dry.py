@@ -116,3 +116,18 @@ def test_cheap_shared_producer_is_recomputed_by_each_consumer():
     g = trace_fn(f)
     r = BK.plan_dry(_program(g, {}, [], g.outputs[0], None, len(g.ops)))
     assert len(r["launches"]) == 1 and r["launches"][0].startswith("fused_ew|")
+
+
+def test_scale_after_gemm_becomes_its_alpha():
+    g = trace_fn(lambda: tg.mulScalar(tg.matmul(T("a", [64, 32]), T("b", [32, 48])), 0.125))
+    r = BK.plan_dry(_program(g, {}, [], g.outputs[0], None, len(g.ops)))
+    assert [x.split("|")[0] for x in r["launches"]] == ["matmul"]
+    # the unscaled product is an output too: the scale stays its own launch
+    g2 = trace_fn(lambda: (lambda m: [tg.mulScalar(m, 0.125), m])(tg.matmul(T("a", [64, 32]), T("b", [32, 48]))))
+    r2 = BK.plan_dry(_program(g2, {}, [], g2.outputs[0], None, len(g2.ops)))
+    assert sorted(x.split("|")[0] for x in r2["launches"]) == ["matmul", "mul_scalar"]
+
+
+def test_attention_scores_scale_is_folded():
+    k = kinds(plan("c4"))
+    assert "mul_scalar" not in k[:k.index("softmax_causal_last")]
