@@ -36,7 +36,7 @@ sys.path.insert(0, ROOT)
 from tensorgrad_b200 import configs as CF  # noqa: E402
 
 METRIC = "train samples/sec (GPT d384 L6 T256, config 4)"
-GEMM_DRAM_BYTES_PER_LAUNCH = 10696.4e6 / 132  # ncu capture, profiles/c4_step_launches.md
+GEMM_DRAM_BYTES_PER_LAUNCH = 11342.6e6 / 144  # ncu capture of one step, profiles/c4_step_launches.md
 UNIT = "samples/s"
 
 
@@ -264,7 +264,7 @@ def main():
             "achieved": gemm_fl / (gemm_ms * 1e-3) / 1e12 if gemm_ms > 0 else None, "peak": bf16,
             "unit": "TFLOP/s", "peak_source": f"{src} bf16 dense (MEASURED_PEAKS.json)",
             # DRAM bytes of the GEMM launches of one step: the average per launch of one ncu
-            # capture (profiles/c4_step_launches.md: 10696 MB over 132 gemm_tc launches) times
+            # capture (profiles/c4_step_launches.md: 11343 MB over 144 gemm_tc launches) times
             # this step's GEMM launches; algorithmic operand+output bytes are far lower because
             # operand tiles are re-read from L2, not DRAM
             "traffic": GEMM_DRAM_BYTES_PER_LAUNCH * n_gemm if args.config == "c4" and not args.batch else None,
