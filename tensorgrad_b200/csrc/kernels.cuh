@@ -124,6 +124,9 @@ struct CopyDesc {
   int64_t numel;
 };
 void launch_copy(const CopyDesc& d, const void* in, void* out, cudaStream_t s);
+// Row-strided copy to a new row stride (operand staging for TMA).
+void launch_pad_rows(const float* src, int64_t ld_src, float* dst, int64_t ld_dst, int64_t rows, int64_t cols,
+                     cudaStream_t s);
 void launch_fill(void* out, int64_t n, uint32_t bits, cudaStream_t s);
 void launch_arange(void* out, int64_t n, int dtype, cudaStream_t s);
 void launch_one_hot(const int* idx, void* out, int64_t n_idx, int64_t depth, int dtype, cudaStream_t s);

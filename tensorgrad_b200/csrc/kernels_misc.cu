@@ -407,6 +407,23 @@ void launch_maxpool_grad(const ConvDesc& c, const float* x, const float* dy, flo
     maxpool_grad_kernel<<<grid_for(total), 256, 0, s>>>(c, x, dy, dx);
 }
 
+// dst[r * ld_dst + c] = src[r * ld_src + c] for r < rows, c < cols: an
+// operand copied to 16-byte row strides so TMA can describe it.
+__global__ void __launch_bounds__(256) pad_rows_kernel(const float* __restrict__ src, int64_t ld_src,
+                                                       float* __restrict__ dst, int64_t ld_dst, int64_t rows,
+                                                       int64_t cols) {
+  const int64_t total = rows * cols;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t r = i / cols, c = i - r * cols;
+    dst[r * ld_dst + c] = src[r * ld_src + c];
+  }
+}
+void launch_pad_rows(const float* src, int64_t ld_src, float* dst, int64_t ld_dst, int64_t rows, int64_t cols,
+                     cudaStream_t s) {
+  if (rows <= 0 || cols <= 0) return;
+  pad_rows_kernel<<<grid_for(rows * cols), 256, 0, s>>>(src, ld_src, dst, ld_dst, rows, cols);
+}
+
 // ------------------------------------------------------------ optimizers --
 // One in-place pass over the flat param/grad/moment arenas: reads p, g, m, v
 // once and writes p, m, v once (28 bytes per parameter), float4-wide. Arena

@@ -153,7 +153,14 @@ static int64_t scratch_for(const Program& P, int i, int action) {
     int64_t K = P.T[a].shape.back(), N = os.back(), M = os[os.size() - 2], batch = 1;
     for (size_t d = 0; d + 2 < os.size(); ++d) batch *= os[d];
     // either the batch folds into M (matmul) or stays a batch: same M*N*batch
-    return 4 * std::max(gemm_tc_workspace_floats(M * batch, N, K, 1), gemm_tc_workspace_floats(M, N, K, batch));
+    int64_t f = std::max(gemm_tc_workspace_floats(M * batch, N, K, 1), gemm_tc_workspace_floats(M, N, K, batch));
+    // room to copy both operands to 16-byte row strides (see the GEMM emission)
+    if (M % 4 || N % 4 || K % 4) {
+      auto up4 = [](int64_t v) { return (v + 3) / 4 * 4; };
+      const int64_t m = M * batch;
+      f = (f + 63) / 64 * 64 + std::max(m * up4(K), K * up4(m)) + std::max(N * up4(K), K * up4(N)) + 128;
+    }
+    return 4 * f;
   }
   if (k == "conv2d" || k == "conv2d_input_grad" || k == "conv2d_weight_grad") {
     const auto& O = P.op(i);
@@ -817,11 +824,38 @@ void Graph::emit_launches() {
       }
       g.workspace = scratch;
       g.workspace_floats = (int64_t)scratch_floats;
+      // TMA needs 16-byte aligned bases and row strides. An operand whose
+      // outer stride is not a multiple of 4 floats (a vocabulary of 65) is
+      // first copied to padded rows after the split-K workspace, so the
+      // contraction still runs on the tensor cores.
+      struct Pad { const float* src; int64_t ld_src; float* dst; int64_t ld_dst, rows, cols; };
+      std::vector<Pad> pads;
+      if (g.batch == 1 && g.M * g.N * g.K >= (int64_t)64 * 64 * 64 && g.K >= 16) {
+        const int64_t wsf = (gemm_tc_workspace_floats(g.M, g.N, g.K, 1) + 63) / 64 * 64;
+        float* next = scratch + wsf;
+        auto up4 = [](int64_t v) { return (v + 3) / 4 * 4; };
+        auto stage = [&](const float*& p, int64_t& s_outer, int64_t s_inner, int64_t outer, int64_t inner) {
+          if (s_inner != 1) return;
+          if (s_outer % 4 == 0 && !(reinterpret_cast<uintptr_t>(p) & 15)) return;
+          const int64_t ld = up4(inner);
+          pads.push_back({p, s_outer, next, ld, outer, inner});
+          p = next;
+          s_outer = ld;
+          next += (outer * ld + 63) / 64 * 64;
+        };
+        if (g.lda_k == 1) stage(g.A, g.lda_m, g.lda_k, g.M, g.K); else stage(g.A, g.lda_k, g.lda_m, g.K, g.M);
+        if (g.ldb_k == 1) stage(g.B, g.ldb_n, g.ldb_k, g.N, g.K); else stage(g.B, g.ldb_k, g.ldb_n, g.K, g.N);
+        if (next > scratch + scratch_floats) throw TgError("Error", "internal: scratch too small for GEMM staging");
+        if (!pads.empty()) g.workspace_floats = wsf;
+      }
       char label[160];
-      snprintf(label, sizeof label, "%s|M=%lld N=%lld K=%lld b=%lld A%s B%s", k.c_str(), (long long)g.M,
+      snprintf(label, sizeof label, "%s|M=%lld N=%lld K=%lld b=%lld A%s B%s%s", k.c_str(), (long long)g.M,
                (long long)g.N, (long long)g.K, (long long)g.batch, g.lda_k == 1 ? "k" : "mn",
-               g.ldb_k == 1 ? "k" : "mn");
-      add(label, [g](cudaStream_t s) { if (!launch_gemm_tc(g, s)) launch_gemm_simt(g, s); });
+               g.ldb_k == 1 ? "k" : "mn", pads.empty() ? "" : " padded");
+      add(label, [g, pads](cudaStream_t s) {
+        for (const Pad& p : pads) launch_pad_rows(p.src, p.ld_src, p.dst, p.ld_dst, p.rows, p.cols, s);
+        if (!launch_gemm_tc(g, s)) launch_gemm_simt(g, s);
+      });
       continue;
     }
     // ---------------------------------------------------------- layout --

@@ -1,6 +1,8 @@
 """tcgen05 3xTF32 GEMM parity: every operand layout the planner produces
 (A and B each K-major or MN-major), ragged tiles, batched head views, and a
-large-K reduction, against the f64 oracle at the op tolerance."""
+large-K reduction, against the f64 oracle at the op tolerance. Row strides
+that are not a multiple of 16 bytes (a vocabulary of 65 or 70) are staged into
+padded copies before the tensor-core GEMM."""
 import numpy as np
 import pytest
 
@@ -13,7 +15,8 @@ pytestmark = pytest.mark.gpu
 
 
 @pytest.mark.parametrize("ta,tb", [(False, False), (False, True), (True, False), (True, True)])
-@pytest.mark.parametrize("M,K,N", [(300, 200, 260), (128, 64, 128), (1000, 96, 70), (256, 200, 30), (256, 30, 200)])
+@pytest.mark.parametrize("M,K,N", [(300, 200, 260), (128, 64, 128), (1000, 96, 70), (256, 200, 30), (256, 30, 200),
+                                   (2048, 384, 65), (2048, 65, 384), (384, 4096, 65)])
 def test_gemm_layouts(ctx, ta, tb, M, K, N):
     a = rnd([K, M] if ta else [M, K], 40)
     b = rnd([N, K] if tb else [K, N], 41)
