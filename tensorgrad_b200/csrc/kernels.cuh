@@ -124,6 +124,25 @@ struct CopyDesc {
   int64_t numel;
 };
 void launch_copy(const CopyDesc& d, const void* in, void* out, cudaStream_t s);
+// Fused causal attention (kernels_attn.cu). A view addresses element
+// (b, h, t, c) at p[b*s0 + h*s1 + t*s2 + c*s3].
+struct AttnView { float* p; int64_t s0, s1, s2, s3; };
+struct AttnParams {
+  int B, H, T, D;
+  AttnView q, k, v, o, dout, dq, dk, dv;
+  float* ml;       // [B*H*T][2]: each query row's max and sum (forward writes, backward reads)
+  float* dv_row;   // [B*H*T]: rowsum(dO * O)
+  float* ds;       // dS rows [B*H*T][ds_ld]; only blocks on or below the diagonal are written
+  int64_t ds_ld;
+  float scale, p, keep_scale;
+  uint32_t salt;   // dropout salt, already mixed as the elementwise dropout mixes it
+  int dropout;
+  const int* seed;
+  int64_t drop_off;
+};
+bool attn_supported_dim(int d);
+void launch_attn_fwd(const AttnParams& P, cudaStream_t s);
+void launch_attn_bwd(const AttnParams& P, cudaStream_t s);
 // Row-strided copy to a new row stride (operand staging for TMA).
 void launch_pad_rows(const float* src, int64_t ld_src, float* dst, int64_t ld_dst, int64_t rows, int64_t cols,
                      cudaStream_t s);

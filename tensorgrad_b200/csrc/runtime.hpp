@@ -11,6 +11,7 @@
 #include <cstdlib>
 #include <functional>
 #include <map>
+#include <set>
 #include <memory>
 #include <stdexcept>
 #include <string>
@@ -182,6 +183,23 @@ class Graph {
   std::vector<StorageLoc> loc_;      // per root tensor
   std::vector<int> op_done_;         // ops folded away
   std::vector<float> gemm_alpha_;    // per GEMM op: output scale folded in from a following mul_scalar
+  // Fused causal attention blocks (plan_attention). Anchor ops carry action
+  // 110 (forward: the PV GEMM) or 111 (backward: the first of its gradient
+  // GEMMs, which writes dQ, dK, dV and dS); the other ops of a block are done.
+  struct AttnBlock {
+    int q, k, kt, v, o;            // forward tensors (k: the key view under the K^T permute)
+    int dout, dv, ds, dq, dkt;     // backward tensors, -1 for a forward-only block
+    int ml, rowdot;                // tensors whose storage holds (m, l) per row and rowsum(dO * O)
+    int p_t;                       // the probabilities tensor (dropout index space)
+    float scale, p, keep_scale;
+    uint32_t salt;
+    bool dropout;
+  };
+  std::vector<AttnBlock> attn_;
+  std::map<int, int> attn_of_;                         // anchor op -> block
+  std::map<int, std::pair<std::vector<int>, std::vector<int>>> fused_io_;  // op -> (reads, writes) for liveness
+  std::map<int, int64_t> bytes_override_;              // root -> bytes, for holders smaller than their tensor
+  void plan_attention(const std::set<int>& observable);
   // Fused elementwise groups. A group is rooted at the op whose output it
   // writes: its last elementwise member, or a reduction that consumes it.
   struct EwGroup {

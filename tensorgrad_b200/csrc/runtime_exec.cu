@@ -217,6 +217,17 @@ void Graph::plan_storage() {
     // An absorbed elementwise op has no output; the groups that evaluate it
     // read its operands at their own positions.
     if (ew_is_absorbed(i)) continue;
+    auto fio = fused_io_.find(i);
+    if (fio != fused_io_.end()) {  // a fused block: its own read and write sets
+      for (int w : fio->second.second) {
+        const int r = views_[w].root;
+        used[r] = 1;
+        if (def[r] < 0 || i < def[r]) def[r] = i;
+        end[r] = std::max(end[r], i);
+      }
+      for (int t : fio->second.first) touch(t, i);
+      continue;
+    }
     int o = P.out[i];
     // The op writes its output's root: its own storage, or (for a GEMM or
     // permute writing straight into a later permute's layout) that root.
@@ -250,7 +261,8 @@ void Graph::plan_storage() {
   auto place = [&](int t, int arena, int64_t off) {
     loc_[t].arena = arena;
     loc_[t].off = off;
-    loc_[t].bytes = std::max<int64_t>(4, P.T[t].numel * 4);
+    auto bo = bytes_override_.find(t);
+    loc_[t].bytes = bo != bytes_override_.end() ? bo->second : std::max<int64_t>(4, P.T[t].numel * 4);
   };
   auto bump_place = [&](int t, int arena) {
     place(t, arena, bump[arena]);
@@ -576,6 +588,40 @@ void Graph::emit_launches() {
     const auto& O = P.op(i);
     int o = P.out[i];
     const auto& os = P.T[o].shape;
+    if (action_[i] == 110 || action_[i] == 111) {
+      const AttnBlock& A = attn_[attn_of_.at(i)];
+      auto aview = [&](int t, bool swap_last) {
+        const TView& v = views_[t];
+        AttnView a{reinterpret_cast<float*>(ptr(t)), v.strides[0], v.strides[1], v.strides[2], v.strides[3]};
+        if (swap_last) std::swap(a.s2, a.s3);
+        return a;
+      };
+      const auto& qs = P.T[A.q].shape;
+      AttnParams ap{};
+      ap.B = (int)qs[0]; ap.H = (int)qs[1]; ap.T = (int)qs[2]; ap.D = (int)qs[3];
+      ap.q = aview(A.q, false); ap.k = aview(A.k, false); ap.v = aview(A.v, false); ap.o = aview(A.o, false);
+      ap.ml = reinterpret_cast<float*>(ptr(A.ml));
+      ap.scale = A.scale; ap.p = A.p; ap.keep_scale = A.keep_scale; ap.salt = A.salt;
+      ap.dropout = A.dropout ? 1 : 0;
+      ap.seed = A.dropout ? seed_ptr : nullptr;
+      ap.drop_off = (int64_t)ctx->rank * P.T[A.p_t].numel;
+      char label[96];
+      snprintf(label, sizeof label, "%s|B=%d H=%d T=%d D=%d", action_[i] == 110 ? "attn_fwd" : "attn_bwd", ap.B, ap.H,
+               ap.T, ap.D);
+      if (action_[i] == 110) {
+        add(label, [ap](cudaStream_t s) { launch_attn_fwd(ap, s); });
+      } else {
+        ap.dout = aview(A.dout, false);
+        ap.dq = aview(A.dq, false);
+        ap.dk = aview(A.dkt, true);
+        ap.dv = aview(A.dv, false);
+        ap.dv_row = reinterpret_cast<float*>(ptr(A.rowdot));
+        ap.ds = reinterpret_cast<float*>(ptr(A.ds));
+        ap.ds_ld = ap.T;
+        add(label, [ap](cudaStream_t s) { launch_attn_bwd(ap, s); });
+      }
+      continue;
+    }
     if (action_[i] == 100) {
       int a = O["a"].i32(), b = O["b"].i32();
       int idx = P.op(P.producer[a])["indices"].i32();

@@ -255,6 +255,8 @@ void Graph::plan_views() {
     op_done_[i] = 1;
   }
 
+  plan_attention(observable);
+
   // A scale whose input only a GEMM writes and nothing else reads becomes
   // that GEMM's alpha: the GEMM stores alpha * acc, rounded once as the
   // mul_scalar would, straight into the scaled tensor's storage (attention's
@@ -430,6 +432,179 @@ void Graph::plan_optimizer() {
     if (dec) n_decay_ = off;
   }
   flat_floats_ = off;
+}
+
+}  // namespace tg
+
+namespace tg {
+
+// Causal attention blocks, matched on the op chain the tracer and autodiff
+// emit (src/ops.ts softmaxCausal and dropout, src/grad.ts rules for matmul,
+// softmaxCausal, dropout and mulScalar):
+//
+//   s = matmul_batched(q, permute(k, swap)), s2 = mul_scalar(s, c),
+//   p = softmax_causal_last(s2), pd = dropout(p) (optional), o = matmul_batched(pd, v)
+//
+// and, when the graph trains, the gradient ops
+//
+//   dpd = matmul_batched(dO, permute(v)), dv = matmul_batched(permute(pd), dO),
+//   dp = dropout(dpd) (same p and salt), r = sum_last(mul(dp, p)),
+//   ds = mul_scalar(mul(sub(dp, broadcast(reshape(r))), p), c),
+//   dq = matmul_batched(ds, permute(permute(k))), dkt = matmul_batched(permute(q), ds).
+//
+// Every intermediate (s, s2, p, pd, dpd, dp, ...) must be read by exactly
+// these ops and be unobservable (not captured, not an output); otherwise the
+// block runs unfused. Head dims 16, 32 and 64 are fused.
+//
+// The fused kernels never materialise the [B, H, T, T] scores and
+// probabilities; measured on B200 they take about the time of the unfused
+// chain (tensor-core GEMMs plus memory-bound passes) at T = 1024 and longer
+// below it. So by default a block is fused when one probabilities tensor
+// would take at least 1 GiB; TG_ATTN_FUSE=1 fuses every matching block,
+// TG_ATTN_FUSE=0 none.
+void Graph::plan_attention(const std::set<int>& observable) {
+  const char* env = getenv("TG_ATTN_FUSE");
+  const int mode = env && env[0] == '1' ? 1 : (env && env[0] == '0' ? 0 : -1);
+  if (mode == 0) return;
+  const int nO = (int)P.ops.size();
+  auto kind_is = [&](int op, const char* k) { return op >= 0 && P.kind[op] == k; };
+  auto only = [&](int t, std::initializer_list<int> ops) {
+    if (observable.count(t)) return false;
+    std::set<int> want(ops), got(P.consumers[t].begin(), P.consumers[t].end());
+    return want == got && P.consumers[t].size() == want.size();
+  };
+  auto swap_perm = [&](int op) {
+    if (!kind_is(op, "permute")) return false;
+    const auto& pv = P.op(op)["perm"].a;
+    return pv.size() == 4 && pv[0].i32() == 0 && pv[1].i32() == 1 && pv[2].i32() == 3 && pv[3].i32() == 2;
+  };
+  auto in = [&](int op, const char* f) { return P.op(op)[f].i32(); };
+  auto rank4 = [&](int t) { return P.T[t].shape.size() == 4 && !views_[t].onehot; };
+  auto consumer_of_kind = [&](int t, const char* k) {
+    for (int c : P.consumers[t]) if (kind_is(c, k)) return c;
+    return -1;
+  };
+
+  for (int f5 = 0; f5 < nO; ++f5) {
+    if (op_done_[f5] || action_[f5] != 0 || !kind_is(f5, "matmul_batched")) continue;
+    const int pd = in(f5, "a"), v = in(f5, "b"), o = P.out[f5];
+    if (!rank4(pd) || !rank4(v) || !rank4(o)) continue;
+    int f4 = P.producer[pd], p_t = pd;
+    const bool drop = kind_is(f4, "dropout");
+    if (drop) p_t = in(f4, "a");
+    const int f3 = P.producer[p_t];
+    if (!kind_is(f3, "softmax_causal_last")) continue;
+    const int s2 = in(f3, "a"), f2 = P.producer[s2];
+    if (!kind_is(f2, "mul_scalar") || !only(s2, {f3})) continue;
+    const int s = in(f2, "a"), f1 = P.producer[s];
+    if (!kind_is(f1, "matmul_batched") || !only(s, {f2}) || op_done_[f1]) continue;
+    const int q = in(f1, "a"), kt = in(f1, "b");
+    const int fk = P.producer[kt];
+    if (!swap_perm(fk) || !rank4(q)) continue;
+    const int k = in(fk, "a");
+    const auto& qs = P.T[q].shape;
+    const int64_t Bn = qs[0], Hn = qs[1], Tn = qs[2], Dn = qs[3];
+    if (!attn_supported_dim((int)Dn) || P.T[k].shape != qs || P.T[v].shape != qs) continue;
+    if (P.T[p_t].shape != std::vector<int64_t>{Bn, Hn, Tn, Tn}) continue;
+    if (mode < 0 && P.T[p_t].numel * 4 < ((int64_t)1 << 30)) continue;
+    const float scale = (float)P.op(f2)["scalar"].num();
+
+    AttnBlock A{};
+    A.q = q; A.k = k; A.kt = kt; A.v = v; A.o = o;
+    A.dout = A.dv = A.ds = A.dq = A.dkt = -1;
+    A.ml = s; A.p_t = p_t; A.scale = scale; A.dropout = drop;
+    A.p = drop ? f32_lit8(P.op(f4)["p"].num()) : 0.f;
+    A.keep_scale = drop ? f32_lit8(1.0 / (1.0 - P.op(f4)["p"].num())) : 1.f;
+    A.salt = drop ? (uint32_t)(((uint64_t)P.op(f4)["salt"].i64() * 0x9E3779B1ull) & 0xFFFFFFFFull) : 0u;
+    std::vector<int> done = {f1, f2, f3};
+    if (drop) done.push_back(f4);
+
+    // backward, if the probabilities are read beyond the forward
+    const bool fwd_only = drop ? (only(p_t, {f4}) && only(pd, {f5})) : only(p_t, {f5});
+    int bwd = -1;
+    if (!fwd_only) {
+      bool ok = true;
+      // dv = matmul_batched(permute(pd), dO)
+      int pdt_op = -1;
+      for (int c : P.consumers[pd]) if (c != f5 && swap_perm(c)) pdt_op = c;
+      ok = ok && swap_perm(pdt_op) && (drop ? only(pd, {f5, pdt_op}) : true);
+      const int pdt = ok ? P.out[pdt_op] : -1;
+      const int bdv = ok ? consumer_of_kind(pdt, "matmul_batched") : -1;
+      ok = ok && bdv >= 0 && only(pdt, {bdv}) && in(bdv, "a") == pdt;
+      const int dO = ok ? in(bdv, "b") : -1;
+      // dpd = matmul_batched(dO, permute(v))
+      int bdp = -1;
+      if (ok)
+        for (int c : P.consumers[dO])
+          if (kind_is(c, "matmul_batched") && in(c, "a") == dO && swap_perm(P.producer[in(c, "b")]) &&
+              in(P.producer[in(c, "b")], "a") == v)
+            bdp = c;
+      ok = ok && bdp >= 0;
+      const int dpd = ok ? P.out[bdp] : -1;
+      int dp = dpd, bdrop = -1;
+      if (ok && drop) {
+        bdrop = consumer_of_kind(dpd, "dropout");
+        ok = bdrop >= 0 && only(dpd, {bdrop}) && P.op(bdrop)["salt"].i64() == P.op(f4)["salt"].i64() &&
+             P.op(bdrop)["p"].num() == P.op(f4)["p"].num();
+        dp = ok ? P.out[bdrop] : -1;
+      }
+      // r = sum_last(mul(dp, p)); ds = mul_scalar(mul(sub(dp, broadcast(reshape(r))), p), c)
+      int m1 = -1, sb = -1;
+      if (ok)
+        for (int c : P.consumers[dp]) {
+          if (kind_is(c, "mul")) m1 = c;
+          if (kind_is(c, "sub") && in(c, "a") == dp) sb = c;
+        }
+      ok = ok && m1 >= 0 && sb >= 0 && only(dp, {m1, sb});
+      ok = ok && ((in(m1, "a") == dp && in(m1, "b") == p_t) || (in(m1, "b") == dp && in(m1, "a") == p_t));
+      const int rs = ok ? consumer_of_kind(P.out[m1], "sum_last") : -1;
+      ok = ok && rs >= 0 && only(P.out[m1], {rs});
+      const int rr = ok ? consumer_of_kind(P.out[rs], "reshape") : -1;
+      ok = ok && rr >= 0 && only(P.out[rs], {rr});
+      const int rb = ok ? consumer_of_kind(P.out[rr], "broadcast_to") : -1;
+      ok = ok && rb >= 0 && only(P.out[rr], {rb}) && only(P.out[rb], {sb}) && in(sb, "b") == P.out[rb];
+      const int m2 = ok ? consumer_of_kind(P.out[sb], "mul") : -1;
+      ok = ok && m2 >= 0 && only(P.out[sb], {m2}) &&
+           ((in(m2, "a") == P.out[sb] && in(m2, "b") == p_t) || (in(m2, "b") == P.out[sb] && in(m2, "a") == p_t));
+      const int ms = ok ? consumer_of_kind(P.out[m2], "mul_scalar") : -1;
+      ok = ok && ms >= 0 && only(P.out[m2], {ms}) && (float)P.op(ms)["scalar"].num() == scale;
+      const int ds = ok ? P.out[ms] : -1;
+      // dq = matmul_batched(ds, permute(kt)), dkt = matmul_batched(permute(q), ds)
+      int bdq = -1, bdk = -1;
+      if (ok)
+        for (int c : P.consumers[ds]) {
+          if (!kind_is(c, "matmul_batched")) continue;
+          if (in(c, "a") == ds && swap_perm(P.producer[in(c, "b")]) && in(P.producer[in(c, "b")], "a") == kt) bdq = c;
+          if (in(c, "b") == ds && swap_perm(P.producer[in(c, "a")]) && in(P.producer[in(c, "a")], "a") == q) bdk = c;
+        }
+      ok = ok && bdq >= 0 && bdk >= 0 && only(ds, {bdq, bdk});
+      ok = ok && (drop ? only(p_t, {f4, m1, m2}) : only(p_t, {f5, pdt_op, m1, m2}));
+      // dS is written as full [B, H, T, T] rows
+      ok = ok && views_[ds].root == ds && views_[ds].contiguous && views_[ds].off == 0;
+      ok = ok && rank4(dO) && rank4(P.out[bdv]) && rank4(P.out[bdq]) && rank4(P.out[bdk]);
+      if (!ok) continue;
+      A.dout = dO; A.dv = P.out[bdv]; A.ds = ds; A.dq = P.out[bdq]; A.dkt = P.out[bdk];
+      A.rowdot = P.out[rs];
+      for (int x : {bdv, m1, rs, rr, rb, sb, m2, ms, bdk}) done.push_back(x);
+      if (drop) done.push_back(bdrop);
+      bwd = std::min({bdp, bdv, bdk});
+      for (int x : {bdp, bdq}) if (x != bwd) done.push_back(x);
+    }
+    // commit
+    const int id = (int)attn_.size();
+    attn_.push_back(A);
+    for (int x : done) if (x != bwd) op_done_[x] = 1;
+    action_[f5] = 110;
+    attn_of_[f5] = id;
+    fused_io_[f5] = {{q, k, v}, {o, s}};
+    bytes_override_[s] = 2 * Bn * Hn * Tn * 4;
+    if (bwd >= 0) {
+      op_done_[bwd] = 0;
+      action_[bwd] = 111;
+      attn_of_[bwd] = id;
+      fused_io_[bwd] = {{q, k, v, o, A.dout, s}, {A.dv, A.ds, A.dkt, A.dq, A.rowdot}};
+    }
+  }
 }
 
 }  // namespace tg

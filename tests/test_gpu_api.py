@@ -74,7 +74,10 @@ def _fwd_ref(model, forward, tokens, params):
     return vals[prog["loss"]]
 
 
-def test_attach_shares_params_and_resolves_parametric_batch(ctx):
+@pytest.mark.parametrize("fuse", ["0", "1"])
+def test_attach_shares_params_and_resolves_parametric_batch(ctx, fuse, monkeypatch):
+    # "1": the forward graphs' attention runs as the fused forward kernel
+    monkeypatch.setenv("TG_ATTN_FUSE", fuse)
     w, t = _train(ctx, seed=3, dropout=0.0)
     T = w.extra["T"]
     logits = t.attach(lambda m, x: CF.gpt_logits(m, x["tokens"]),
@@ -101,6 +104,8 @@ def test_attach_shares_params_and_resolves_parametric_batch(ctx):
         np.testing.assert_array_equal(am[clear], np.argmax(ref, -1)[clear])
 
     check(2, 0)
+    assert ("attn_fwd" in [x.split("|")[0] for x in logits.graph_for(
+        {"tokens": np.zeros((2, T), np.int32)}).launch_list()]) == (fuse == "1")
     check(7, 11)                 # a second resolved shape evicts the first (LRU of 1)
     assert len(logits._cache) == 1
     _step(t, _batch(w, 0))       # the attached graphs read the trainer's updated params

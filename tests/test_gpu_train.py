@@ -18,6 +18,7 @@ trajectories that slowly decorrelate:
   previous state, per element with the test_gpu_ops bound.
 """
 import math
+import os
 
 import numpy as np
 import pytest
@@ -40,8 +41,8 @@ TINY = {
 }
 
 
-def setup(ctx, name):
-    w = CF.workload(name, **TINY[name])
+def setup(ctx, name, **over):
+    w = CF.workload(name, **{**TINY[name], **over})
     B = w.global_batch
     ir = build_training_ir(w.make_model(), w.loss, w.inputs(B), w.optimizer)
     init = initial_params(ir.graph, ir.materialized.initFns, CF.PARAM_SEED)
@@ -105,7 +106,29 @@ def _decayed(program):
 
 @pytest.mark.parametrize("name", ["c1", "c2", "c3", "c4", "c5"])
 def test_train_parity(ctx, name, steps=5):
-    w, ir, dg, orc, data = setup(ctx, name)
+    _parity(ctx, name, steps)
+
+
+@pytest.mark.parametrize("over", [
+    dict(T=200, D=128, heads=2, layers=1, batch=2, dropout=0.2),  # head dim 64, ragged last block
+    dict(T=128, D=128, heads=2, layers=1, batch=2, dropout=0.0),  # no dropout op in the chain
+    dict(T=96, D=64, heads=2, layers=2, batch=3, dropout=0.2),    # head dim 32
+])
+def test_fused_attention_train_parity(ctx, over, monkeypatch):
+    """GPT steps whose attention runs as the fused flash-style kernels
+    (forward, and dK/dV/dS plus dQ backward) against the oracle's unfused
+    graph: loss, every gradient and the optimizer update."""
+    monkeypatch.setenv("TG_ATTN_FUSE", "1")
+    _parity(ctx, "c4", 2, **over)
+
+
+def _parity(ctx, name, steps, **over):
+    w, ir, dg, orc, data = setup(ctx, name, **over)
+    if name in ("c4", "c5"):
+        kinds = [x.split("|")[0] for x in dg.launch_list()]
+        fused = os.environ.get("TG_ATTN_FUSE") == "1"
+        assert ("attn_fwd" in kinds and "attn_bwd" in kinds) == fused
+        assert ("softmax_causal_last" in kinds) != fused
     shapes = {n: tuple(t.shape) for n, t in ir.paramGrads.items()}
     try:
         for t in range(1, steps + 1):

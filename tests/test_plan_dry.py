@@ -128,6 +128,35 @@ def test_scale_after_gemm_becomes_its_alpha():
     assert sorted(x.split("|")[0] for x in r2["launches"]) == ["matmul", "mul_scalar"]
 
 
-def test_attention_scores_scale_is_folded():
+@pytest.fixture
+def fuse_attention(monkeypatch):
+    monkeypatch.setenv("TG_ATTN_FUSE", "1")
+
+
+def test_attention_fusion_default_follows_scores_size():
+    # 4 x 2 x 16 x 16 probabilities: far below the 1 GiB default threshold
+    assert "attn_fwd" not in kinds(plan("c4"))
+
+
+def test_attention_blocks_are_fused(fuse_attention):
     k = kinds(plan("c4"))
-    assert "mul_scalar" not in k[:k.index("softmax_causal_last")]
+    layers = TINY["c4"]["layers"]
+    assert k.count("attn_fwd") == layers and k.count("attn_bwd") == layers
+    assert "matmul_batched" not in k and "softmax_causal_last" not in k
+
+
+def _attention(observe_scores):
+    def f():
+        q, kk, v = T("q", [2, 2, 64, 64]), T("k", [2, 2, 64, 64]), T("v", [2, 2, 64, 64])
+        s = tg.mulScalar(tg.matmul(q, tg.swapAxes(kk, -1, -2)), 0.125)
+        o = tg.matmul(tg.softmaxCausal(s), v)
+        return [o, s] if observe_scores else o
+    g = trace_fn(f)
+    return BK.plan_dry(_program(g, {}, [], g.outputs[0], None, len(g.ops)))
+
+
+def test_observed_scores_keep_attention_unfused(fuse_attention):
+    assert kinds(_attention(False)) == ["attn_fwd"]
+    # the scores are an output: the chain runs op by op, the scale folded
+    # into the scores GEMM
+    assert kinds(_attention(True)) == ["matmul_batched", "softmax_causal_last", "matmul_batched"]
