@@ -144,15 +144,16 @@ def run_reference(args, w):
         v, dt = cpu_baseline(w, sample, threads)
         vals.append(v)
     v = float(np.median(vals))
-    line = {"impl": "reference", "metric": METRIC, "value": v, "unit": UNIT, "n_gpus": args.gpus,
+    metric = METRIC if args.config == "c4" else f"train samples/sec ({w.name}, config {args.config[1:]})"
+    line = {"impl": "reference", "metric": metric, "value": v, "unit": UNIT, "n_gpus": args.gpus,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000.0 * sample / v,
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
             "data": "synthetic (mulberry32 seed 1234 tokens)",
             "config": {"workload": w.name, "global_batch": sample, "seq_len": w.extra.get("T"),
                        "parallelism": "cpu"},
             "cpu_baseline": {"value": v, "unit": UNIT, "cores": threads, "kind": "port",
-                             "sample": f"one training step at batch {sample} (T=256, full model) per timed step; "
-                                       "numpy restatement of the reference CPU evaluator"},
+                             "sample": f"one training step of {w.name} at batch {sample} (full model) per timed "
+                                       "step; numpy restatement of the reference CPU evaluator"},
             "e2e": {"value": v, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
 
