@@ -206,10 +206,16 @@ class Graph {
     std::vector<int> members;  // elementwise ops evaluated per element, ascending
     int root = -1;             // op whose output the launch writes
     int red = -1;              // the root when it is a reduction (sum_last, mean_last, sum_to_shape)
+    // Row reductions only: groups of one value per row that read the
+    // reduction's result, evaluated by the same kernel after the row sum
+    // (their ops merged, ascending); each post root's output is written too.
+    std::vector<int> post;
+    std::vector<int> post_roots;
   };
   std::vector<EwGroup> ew_groups_;
   std::vector<int> ew_group_;        // per op: group index when the op roots a group, else -1
   std::vector<char> ew_absorbed_;    // per op: value computed inside the groups that use it (no storage)
+  std::vector<char> ew_post_;        // per op: absorbed as a row reduction's post op, output still stored
   bool jit_ = false;                 // fused elementwise groups compiled at plan time
   std::vector<std::string> jit_sources_;  // generated kernel sources (planning-only contexts)
   void* arena_[AR_COUNT] = {};

@@ -246,10 +246,23 @@ void Graph::plan_storage() {
       continue;
     }
     const int g = ew_group_of(i);
-    if (g >= 0)
+    if (g >= 0) {
       for (int m : ew_groups_[g].members)
         for (int t : P.op_inputs[m])
           if (!ew_internal(t)) touch(t, i);
+      const EwGroup& G = ew_groups_[g];
+      for (int pr : G.post_roots) {  // the kernel also writes the post ops' results
+        const int r = views_[P.out[pr]].root;
+        used[r] = 1;
+        if (def[r] < 0 || i < def[r]) def[r] = i;
+        end[r] = std::max(end[r], i);
+      }
+      if (!G.post_roots.empty()) {
+        for (int m : G.post)
+          for (int t : P.op_inputs[m])
+            if (!ew_internal(t)) touch(t, i);
+      }
+    }
     for (int t : P.op_inputs[i])
       if (!ew_internal(t)) touch(t, i);
   }

@@ -100,7 +100,7 @@ constexpr int kMaxGroupOps = 48;
 bool Graph::ew_internal(int t) const {
   if (ew_absorbed_.empty()) return false;
   const int p = P.producer[t];
-  return p >= 0 && ew_absorbed_[p];
+  return p >= 0 && ew_absorbed_[p] && !ew_post_[p];
 }
 
 namespace {
@@ -141,6 +141,7 @@ void Graph::plan_fusion() {
   const int nO = (int)P.ops.size();
   ew_group_.assign(nO, -1);
   ew_absorbed_.assign(nO, 0);
+  ew_post_.assign(nO, 0);
   ew_groups_.clear();
   jit_ = jit_enabled();
   if (!jit_) return;
@@ -256,6 +257,55 @@ void Graph::plan_fusion() {
     }
     ew_group_[g.root] = (int)ew_groups_.size();
     ew_groups_.push_back(std::move(g));
+  }
+
+  // Post ops: a group with one value per row that reads a warp-per-row
+  // reduction's result, and otherwise only per-row tensors produced earlier
+  // or scalars, is evaluated by lane 0 of the reduction kernel after the sum
+  // (LayerNorm's eps and sqrt on the variance, the row terms of its
+  // gradient). Each such group saves a launch; the reduction's own result is
+  // still written.
+  std::map<int, std::vector<int>> owners;  // member op -> groups containing it
+  for (size_t gi = 0; gi < ew_groups_.size(); ++gi)
+    for (int m : ew_groups_[gi].members) owners[m].push_back((int)gi);
+  for (size_t ri = 0; ri < ew_groups_.size(); ++ri) {
+    EwGroup& R = ew_groups_[ri];
+    if (R.red < 0) continue;
+    int64_t rows = 0, len = 0;
+    if (red_shape(P, R.red, &rows, &len) != RED_ROW) continue;
+    const int t = P.out[R.red];
+    if (P.T[t].numel != rows || !views_[t].contiguous || views_[t].onehot) continue;
+    std::set<int> post(R.post.begin(), R.post.end());
+    for (int c : P.consumers[t]) {
+      auto it = owners.find(c);
+      if (it == owners.end()) continue;
+      for (int ci : it->second) {
+        EwGroup& C = ew_groups_[ci];
+        if (ci == (int)ri || C.red >= 0 || C.root < 0 || ew_group_[C.root] != ci) continue;
+        if (P.T[P.out[C.root]].numel != rows || side(C.root) != side(R.red)) continue;
+        const std::set<int> cm(C.members.begin(), C.members.end());
+        bool ok = (int)(post.size() + C.members.size()) <= kMaxGroupOps && R.post_roots.size() < 4;
+        for (int m : C.members) {
+          if (P.kind[m] == "dropout" || P.kind[m] == "where_causal") ok = false;
+          if (P.T[P.out[m]].numel != rows) ok = false;
+          for (int x : ew_operands(P, m)) {
+            if (x == t || cm.count(P.producer[x])) continue;
+            const TView& vx = views_[x];
+            const bool stored =
+                vx.contiguous && !vx.onehot && vx.root == x && !ew_internal(x) && P.producer[x] < R.red;
+            if (!stored || (P.T[x].numel != 1 && P.T[x].numel != rows)) ok = false;
+          }
+        }
+        if (!ok) continue;
+        post.insert(C.members.begin(), C.members.end());
+        R.post_roots.push_back(C.root);
+        ew_absorbed_[C.root] = 1;
+        ew_post_[C.root] = 1;
+        ew_group_[C.root] = -1;
+        C.root = -1;
+      }
+    }
+    R.post.assign(post.begin(), post.end());
   }
 }
 
@@ -417,10 +467,46 @@ void Graph::emit_ew_group(int gi, const int* seed_ptr, float* scratch, size_t sc
     }
   }
 
+  // Post ops (row reductions): evaluated by lane 0 on the row's result; their
+  // other inputs are per-row tensors (read at the row) or scalars.
+  std::ostringstream post;
+  const bool has_post = rs == RED_ROW && !G.post_roots.empty();
+  if (has_post) {
+    const int t = P.out[G.red];
+    const std::set<int> pm(G.post.begin(), G.post.end());
+    std::map<int, int> pslot;
+    for (int m : G.post) {
+      std::vector<std::string> a;
+      for (int x : ew_operands(P, m)) {
+        if (x == t || pm.count(P.producer[x])) { a.push_back("v" + std::to_string(x)); continue; }
+        auto it = pslot.find(x);
+        if (it == pslot.end()) {
+          it = pslot.emplace(x, (int)ins.size()).first;
+          EwInput in{};
+          in.ptr = ptr(x);
+          in.mode = P.T[x].numel == 1 ? IN_SCALAR : IN_FULL;
+          ins.push_back(in);
+          post << "      const float y" << it->second << " = __ldg(p" << it->second
+               << (P.T[x].numel == 1 ? ")" : " + r)") << ";\n";
+        }
+        a.push_back("y" + std::to_string(it->second));
+      }
+      const bool int_cmp = (P.kind[m] == "less" || P.kind[m] == "greater") && P.T[ew_operands(P, m)[0]].dtype != F32;
+      post << "      const float v" << P.out[m] << " = " << ew_expr(P, m, a, int_cmp) << ";\n";
+    }
+    for (size_t pr = 0; pr < G.post_roots.size(); ++pr)
+      post << "      out" << 2 + pr << "[r] = v" << P.out[G.post_roots[pr]] << ";\n";
+    label += "+post:";
+    for (int m : G.post) label += P.kind[m] + (m == G.post.back() ? "" : "+");
+  }
+
   std::ostringstream k;
   k << "(";
   for (size_t si = 0; si < ins.size(); ++si) k << "const float* __restrict__ p" << si << ", ";
-  k << "float* __restrict__ out, const int* __restrict__ seedp, i64 drop_off) {\n";
+  k << "float* __restrict__ out, ";
+  if (has_post)
+    for (size_t pr = 0; pr < G.post_roots.size(); ++pr) k << "float* __restrict__ out" << 2 + pr << ", ";
+  k << "const int* __restrict__ seedp, i64 drop_off) {\n";
   k << "  const u32 seed = " << (has_drop ? "seedp ? (u32)(*seedp) : 0u" : "0u") << ";\n";
   k << "  (void)seed; (void)drop_off;\n";
   int64_t nchunk = 1;
@@ -435,7 +521,13 @@ void Graph::emit_ew_group(int gi, const int* seed_ptr, float* scratch, size_t sc
       << " + j;\n";
     k << lane.str() << ops.str() << "      acc += " << value << ";\n    }\n";
     k << "    for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);\n";
-    k << "    if (lane == 0) out[r] = " << (mean ? "__fdiv_rn(acc, " + lit((float)len) + ")" : "acc") << ";\n  }\n}\n";
+    const std::string red = mean ? "__fdiv_rn(acc, " + lit((float)len) + ")" : "acc";
+    if (has_post) {
+      k << "    if (lane == 0) {\n      const float v" << P.out[G.red] << " = " << red << ";\n      out[r] = v"
+        << P.out[G.red] << ";\n" << post.str() << "    }\n  }\n}\n";
+    } else {
+      k << "    if (lane == 0) out[r] = " << red << ";\n  }\n}\n";
+    }
   } else if (rs == RED_COL) {
     // first pass of the deterministic column sum: rows of chunk blockIdx.y in
     // ascending order (the unfused kernel's order); the fold is shared
@@ -492,11 +584,14 @@ void Graph::emit_ew_group(int gi, const int* seed_ptr, float* scratch, size_t sc
   struct Args {
     std::vector<const void*> in;
     void* out;
+    std::vector<void*> outs;  // post roots' outputs
     const int* seed;
     long long drop_off;
   };
   auto A = std::make_shared<Args>();
   for (auto& in : ins) A->in.push_back(in.ptr);
+  if (has_post)
+    for (int pr : G.post_roots) A->outs.push_back(ptr(P.out[pr]));
   A->out = (rs == RED_COL && nchunk > 1) ? static_cast<void*>(scratch) : out;
   A->seed = seed_ptr;
   A->drop_off = (long long)ctx->rank * n;
@@ -523,6 +618,7 @@ void Graph::emit_ew_group(int gi, const int* seed_ptr, float* scratch, size_t sc
     std::vector<void*> args;
     for (auto& p : A->in) args.push_back(const_cast<const void**>(&p));
     args.push_back(&A->out);
+    for (auto& o : A->outs) args.push_back(&o);
     args.push_back(const_cast<const int**>(&A->seed));
     args.push_back(&A->drop_off);
     jit_launch(*fn, gx, gy, tpb, args.data(), s);

@@ -156,6 +156,20 @@ def test_sum_to_shape_trailing(ctx):
     run(ctx, lambda: tg.sumToShape(T("b", [3, 40000]), [3, 1]), {"b": b})
 
 
+def test_layernorm_row_post_ops(ctx):
+    """Row-reduction kernels that also evaluate the per-row values after the
+    sum (eps, sqrt) and write them: LayerNorm forward and a row-term use of
+    the standard deviation."""
+    x = rnd([300, 384], 65, -2, 2)
+
+    def build():
+        X = T("x", [300, 384])
+        d = tg.sub(X, tg.mean(X, -1, keepDims=True))
+        sd = tg.sqrt(tg.addScalar(tg.mean(tg.mul(d, d), -1, keepDims=True), 1e-5))
+        return tg.add(tg.div(d, sd), tg.mul(sd, sd))
+    run(ctx, build, {"x": x})
+
+
 def test_sum_to_shape_middle(ctx):
     """Reduced dims on both sides of the kept ones (the conv bias gradient
     [B, C, H, W] -> [C, 1, 1]), small and at the CNN benchmark's size."""

@@ -160,3 +160,18 @@ def test_observed_scores_keep_attention_unfused(fuse_attention):
     # the scores are an output: the chain runs op by op, the scale folded
     # into the scores GEMM
     assert kinds(_attention(True)) == ["matmul_batched", "softmax_causal_last", "matmul_batched"]
+
+
+def _layernorm(x):
+    d = tg.sub(x, tg.mean(x, -1, keepDims=True))
+    sd = tg.sqrt(tg.addScalar(tg.mean(tg.mul(d, d), -1, keepDims=True), 1e-5))
+    return tg.div(d, sd)
+
+
+def test_row_values_after_a_row_reduction_run_in_its_kernel():
+    """LayerNorm: the eps add and sqrt on the variance run as post ops of the
+    variance's row reduction instead of a launch of their own."""
+    g = trace_fn(lambda: _layernorm(T("x", [64, 48])))
+    k = BK.plan_dry(_program(g, {}, [], g.outputs[0], None, len(g.ops)))["launches"]
+    assert any(x.startswith("fused_red|mean_last") and "post:add_scalar+sqrt" in x for x in k)
+    assert not any(x.startswith("fused_ew|add_scalar+sqrt") for x in k)
