@@ -264,12 +264,12 @@ def main():
     roof = {"bound": "tensor", "kernel": "matmul+matmul_batched (all GEMM launches of one step)",
             "achieved": gemm_fl / (gemm_ms * 1e-3) / 1e12 if gemm_ms > 0 else None, "peak": bf16,
             "unit": "TFLOP/s", "peak_source": f"{src} bf16 dense (MEASURED_PEAKS.json)",
-            # DRAM bytes of the GEMM launches of one step: the average per launch of one ncu
-            # capture (profiles/c4_step_launches.md: 11343 MB over 144 gemm_tc launches) times
-            # this step's GEMM launches; algorithmic operand+output bytes are far lower because
-            # operand tiles are re-read from L2, not DRAM
-            "traffic": GEMM_DRAM_BYTES_PER_LAUNCH * n_gemm if args.config == "c4" and not args.batch else None,
-            "traffic_unit": "bytes per step (GEMM class)"}
+            # DRAM bytes per GEMM launch, averaged over the step's launches in one ncu capture
+            # (profiles/c4_step_launches.md: 11343 MB over 144 gemm_tc launches). "achieved" is
+            # the same average: the step's GEMM flops over its GEMM time.
+            "traffic": GEMM_DRAM_BYTES_PER_LAUNCH if args.config == "c4" and not args.batch else None,
+            "traffic_unit": "bytes per launch (average over the step's GEMM launches)",
+            "gemm_launches_per_step": n_gemm}
     roof["frac"] = roof["achieved"] / bf16 if roof["achieved"] else None
     roof["frac_of_3xtf32_effective"] = roof["achieved"] / (bf16 / 6.0) if roof["achieved"] else None
     roof["dominant_kind"] = dom
