@@ -396,37 +396,44 @@ __global__ void __launch_bounds__(448, 1) gemm_tc_kernel(const __grid_constant__
       // kind::tf32 instruction descriptor: D f32, A/B tf32, K-major, N>>3, M>>4
       const uint32_t idesc = (1u << 4) | (2u << 7) | (2u << 10) | ((uint32_t)(TC_BN >> 3) << 17) |
                              ((uint32_t)(TC_BM >> 4) << 24);
-      int gs = 0, gc = 0;
+      // Everything per stage that does not change is computed here: between
+      // two stages the issuing thread's work leaves the tensor pipe idle (the
+      // MMA queue is about one instruction deep), so the loop keeps only the
+      // barrier wait, 12 MMAs and the commits. Shared-memory descriptors
+      // advance by address >> 4 in their low field (smem < 256 KB, no carry).
+      const uint64_t desc0 = umma_desc(smem_u32(smem) + TC_TILE_BYTES, 16, 1024);
+      const uint32_t a0 = tmem + TC_ACOL;
+      int s = 0, gs = 0;
+      uint32_t ph = 0;
+      int gc = 0;
       for (int64_t u = blockIdx.x; u < P.units && ok; u += gridDim.x) {
         const TcUnit U = tc_unit(P, u);
         for (int it = 0; it < U.nk; ++it, ++gs) {
-          const int s = gs % NS;
           const int c = gc + it / TC_CHUNK, acc = c & 1;
           const bool chunk_start = (it % TC_CHUNK) == 0;
           if (chunk_start && c >= 2 && !mbar_wait(&dempty[acc], (uint32_t)((c - 2) >> 1) & 1u, 5)) {
             ok = false; break;
           }
-          if (!mbar_wait(&conv[s], (uint32_t)(gs / NS) & 1u, 2)) { ok = false; break; }
+          if (!mbar_wait(&conv[s], ph, 2)) { ok = false; break; }
           mark(10, gs);
           asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-          const uint32_t base = smem_u32(smem + s * SB);
-          const uint32_t b_hi = base + TC_TILE_BYTES, b_lo = base + 2 * TC_TILE_BYTES;
-          const uint32_t a_hi = tmem + TC_ACOL + 64u * (uint32_t)s, a_lo = a_hi + 32u;
+          const uint64_t dh = desc0 + (uint64_t)(s * (SB >> 4)), dl = dh + (TC_TILE_BYTES >> 4);
+          const uint32_t a_hi = a0 + 64u * (uint32_t)s, a_lo = a_hi + 32u;
           const uint32_t dacc = tmem + (uint32_t)(acc * TC_BN);
 #pragma unroll
           for (int kk = 0; kk < TC_BK / 8; ++kk) {
             // B: 128 rows of 128 bytes (32 K values), 8-row groups 1 KB apart
-            // (SBO); a K step of 8 advances 32 bytes in the row. A: 8 columns.
-            const uint64_t dBh = umma_desc(b_hi + kk * 32, 16, 1024), dBl = umma_desc(b_lo + kk * 32, 16, 1024);
+            // (SBO); a K step of 8 advances 32 bytes (2 in the address field).
+            // A: 8 TMEM columns.
             const uint32_t first = (chunk_start && kk == 0) ? 0u : 1u;
-            umma_tf32_ts(dacc, a_lo + kk * 8, dBh, idesc, first);
-            umma_tf32_ts(dacc, a_hi + kk * 8, dBl, idesc, 1u);
-            umma_tf32_ts(dacc, a_hi + kk * 8, dBh, idesc, 1u);
+            umma_tf32_ts(dacc, a_lo + kk * 8, dh + 2 * kk, idesc, first);
+            umma_tf32_ts(dacc, a_hi + kk * 8, dl + 2 * kk, idesc, 1u);
+            umma_tf32_ts(dacc, a_hi + kk * 8, dh + 2 * kk, idesc, 1u);
           }
           mark(3, gs);
-          if (blockIdx.x == 0) g_gemm_tc_dbg[2] = gs + 1;
           umma_commit(&empty[s]);  // frees the stage (smem and TMEM A) once these MMAs have read it
           if ((it % TC_CHUNK) == TC_CHUNK - 1 || it == U.nk - 1) umma_commit(&dfull[acc]);
+          if (++s == NS) { s = 0; ph ^= 1u; }
         }
         gc += (U.nk + TC_CHUNK - 1) / TC_CHUNK;
       }
