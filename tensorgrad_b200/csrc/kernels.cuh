@@ -93,6 +93,20 @@ enum RowKind : int { ROW_SUM = 0, ROW_MEAN, ROW_ARGMAX, ROW_LOGSOFTMAX, ROW_SOFT
 void launch_row(int kind, const float* x, void* out, int64_t rows, int64_t D, cudaStream_t s,
                 const int* seed = nullptr, uint32_t salt = 0, float* scratch = nullptr,
                 size_t scratch_floats = 0);
+// softmax_causal rows of D <= 1024 that also write dropout(softmax) to out2:
+// element e of the [rows, D] result keeps when the hash of
+// (seed ^ salt ^ (u32)(drop_off + e)) / 2^32 >= p and is scaled by keep_scale,
+// exactly as the elementwise dropout kernels decide. Returns false (nothing
+// launched) for rows too long for the register path.
+struct RowDropout {
+  float* out2;
+  const int* seed;
+  uint32_t salt;
+  float p, keep_scale;
+  int64_t drop_off;
+};
+bool launch_softmax_causal_dropout(const float* x, float* out, int64_t rows, int64_t D, const RowDropout& d,
+                                   cudaStream_t s);
 // Scratch floats launch_row uses (long-row split path); 0 when none.
 size_t row_scratch_floats(int kind, int64_t rows, int64_t D);
 

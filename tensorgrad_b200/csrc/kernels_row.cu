@@ -233,9 +233,16 @@ size_t row_scratch_floats(int kind, int64_t rows, int64_t D) {
 // registers: one load, a warp max, one exp per element, a warp sum, one
 // store (element j of the row lives in lane j % 32, slot j / 32, so every
 // load and store is a coalesced 128-byte warp access).
-template <int KIND, int NV>
+__device__ __forceinline__ uint32_t pcg_s(uint32_t h) {
+  h = h * 747796405u + 2891336453u;
+  h = ((h >> ((h >> 28u) + 4u)) ^ h) * 277803737u;
+  return (h >> 22u) ^ h;
+}
+
+template <int KIND, int NV, bool DROP = false>
 __global__ void __launch_bounds__(256) row_softmax_reg_kernel(const float* __restrict__ x, float* __restrict__ out,
-                                                              int64_t rows, int64_t D) {
+                                                              int64_t rows, int64_t D,
+                                                              const __grid_constant__ RowDropout drop = RowDropout{}) {
   const int lane = threadIdx.x & 31;
   const int64_t warp = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
@@ -270,10 +277,19 @@ __global__ void __launch_bounds__(256) row_softmax_reg_kernel(const float* __res
         if (j < D) o[j] = v[i] - lz;
       }
     } else {
+      const uint32_t seed = DROP && drop.seed ? (uint32_t)(*drop.seed) : 0u;
 #pragma unroll
       for (int i = 0; i < NV; ++i) {
         const int64_t j = lane + 32 * i;
-        if (j < D) o[j] = j < lim ? __fdiv_rn(v[i], sum) : 0.f;
+        if (j < D) {
+          const float pv = j < lim ? __fdiv_rn(v[i], sum) : 0.f;
+          o[j] = pv;
+          if (DROP) {
+            const uint32_t hsh = pcg_s(seed ^ drop.salt ^ (uint32_t)(drop.drop_off + r * D + j));
+            const float u = __uint2float_rn(hsh) * 2.3283064365386963e-10f;  // exact divide by 2^32
+            drop.out2[r * D + j] = __fmul_rn(pv, u >= drop.p ? drop.keep_scale : 0.f);
+          }
+        }
       }
     }
   }
@@ -291,6 +307,21 @@ static bool launch_softmax_reg(const float* x, float* out, int64_t rows, int64_t
   else if (D <= 512) row_softmax_reg_kernel<KIND, 16><<<g, 256, 0, s>>>(x, out, rows, D);
   else if (D <= 1024) row_softmax_reg_kernel<KIND, 32><<<g, 256, 0, s>>>(x, out, rows, D);
   else return false;
+  return true;
+}
+
+bool launch_softmax_causal_dropout(const float* x, float* out, int64_t rows, int64_t D, const RowDropout& d,
+                                   cudaStream_t s) {
+  if (rows <= 0 || D > 1024) return false;
+  const int64_t blocks = (rows + 7) / 8, cap = (int64_t)device_sm_count() * 16;
+  const unsigned g = (unsigned)(blocks < cap ? blocks : cap);
+  constexpr int K = ROW_SOFTMAX_CAUSAL;
+  if (D <= 32) row_softmax_reg_kernel<K, 1, true><<<g, 256, 0, s>>>(x, out, rows, D, d);
+  else if (D <= 64) row_softmax_reg_kernel<K, 2, true><<<g, 256, 0, s>>>(x, out, rows, D, d);
+  else if (D <= 128) row_softmax_reg_kernel<K, 4, true><<<g, 256, 0, s>>>(x, out, rows, D, d);
+  else if (D <= 256) row_softmax_reg_kernel<K, 8, true><<<g, 256, 0, s>>>(x, out, rows, D, d);
+  else if (D <= 512) row_softmax_reg_kernel<K, 16, true><<<g, 256, 0, s>>>(x, out, rows, D, d);
+  else row_softmax_reg_kernel<K, 32, true><<<g, 256, 0, s>>>(x, out, rows, D, d);
   return true;
 }
 

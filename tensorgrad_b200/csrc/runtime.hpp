@@ -199,6 +199,8 @@ class Graph {
   std::map<int, int> attn_of_;                         // anchor op -> block
   std::map<int, std::pair<std::vector<int>, std::vector<int>>> fused_io_;  // op -> (reads, writes) for liveness
   std::map<int, int64_t> bytes_override_;              // root -> bytes, for holders smaller than their tensor
+  std::map<int, int> softmax_drop_;                    // softmax_causal op -> dropout op it also evaluates
+  std::map<int, std::vector<int>> extra_writes_;       // op -> further tensors its launch writes
   void plan_attention(const std::set<int>& observable);
   // Fused elementwise groups. A group is rooted at the op whose output it
   // writes: its last elementwise member, or a reduction that consumes it.

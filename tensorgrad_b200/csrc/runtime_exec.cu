@@ -265,6 +265,14 @@ void Graph::plan_storage() {
     }
     for (int t : P.op_inputs[i])
       if (!ew_internal(t)) touch(t, i);
+    auto xw = extra_writes_.find(i);
+    if (xw != extra_writes_.end())
+      for (int t : xw->second) {
+        const int r = views_[t].root;
+        used[r] = 1;
+        if (def[r] < 0 || i < def[r]) def[r] = i;
+        end[r] = std::max(end[r], i);
+      }
   }
   for (int t : pinned) used[t] = 1;
   if (P.loss >= 0) { pinned.insert(views_[P.loss].root); used[views_[P.loss].root] = 1; }
@@ -776,6 +784,21 @@ void Graph::emit_launches() {
       void* out = ptr(o);
       const int* sd = k == "categorical_last" ? reinterpret_cast<const int*>(ptr(O["seed"].i32())) : nullptr;
       uint32_t salt = k == "categorical_last" ? (uint32_t)(((uint64_t)O["salt"].i64() * 0x9E3779B1ull) & 0xFFFFFFFFull) : 0;
+      auto sdrop = softmax_drop_.find(i);
+      if (sdrop != softmax_drop_.end()) {  // the softmax also writes its dropout
+        const auto& DO = P.op(sdrop->second);
+        const double pd = DO["p"].num();
+        RowDropout rd{};
+        rd.out2 = reinterpret_cast<float*>(ptr(P.out[sdrop->second]));
+        rd.seed = seed_ptr;
+        rd.salt = (uint32_t)(((uint64_t)DO["salt"].i64() * 0x9E3779B1ull) & 0xFFFFFFFFull);
+        rd.p = f32_lit8(pd);
+        rd.keep_scale = f32_lit8(1.0 / (1.0 - pd));
+        rd.drop_off = (int64_t)ctx->rank * P.T[o].numel;
+        float* fo = reinterpret_cast<float*>(out);
+        add("softmax_causal_last+dropout", [=](cudaStream_t s) { launch_softmax_causal_dropout(x, fo, rows, D, rd, s); });
+        continue;
+      }
       add(k, [=](cudaStream_t s) { launch_row(kind, x, out, rows, D, s, sd, salt, scratch, scratch_floats); });
       continue;
     }

@@ -307,6 +307,32 @@ void Graph::plan_fusion() {
     }
     R.post.assign(post.begin(), post.end());
   }
+
+  // A dropout that is the only member of its group and reads a causal
+  // softmax's result is written by the softmax kernel as a second output
+  // (attention's dropout on the probabilities): one read of the [.., T, T]
+  // tensor less.
+  softmax_drop_.clear();
+  extra_writes_.clear();
+  for (int sm = 0; sm < nO; ++sm) {
+    if (op_done_[sm] || action_[sm] != 0 || P.kind[sm] != "softmax_causal_last") continue;
+    const int pt = P.out[sm];
+    if (P.T[pt].shape.back() > 1024 || views_[pt].root != pt || !views_[pt].contiguous) continue;
+    for (int d : P.consumers[pt]) {
+      const int gi = ew_group_of(d);
+      if (P.kind[d] != "dropout" || gi < 0 || ew_groups_[gi].members != std::vector<int>{d}) continue;
+      const int dt = P.out[d];
+      if (P.T[dt].shape != P.T[pt].shape || views_[dt].root != dt || !views_[dt].contiguous) continue;
+      if (side(d) != side(sm)) continue;
+      softmax_drop_[sm] = d;
+      extra_writes_[sm].push_back(dt);
+      ew_group_[d] = -1;
+      ew_absorbed_[d] = 1;
+      ew_post_[d] = 1;
+      ew_groups_[gi].root = -1;
+      break;
+    }
+  }
 }
 
 namespace {

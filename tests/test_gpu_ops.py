@@ -156,6 +156,15 @@ def test_sum_to_shape_trailing(ctx):
     run(ctx, lambda: tg.sumToShape(T("b", [3, 40000]), [3, 1]), {"b": b})
 
 
+def test_softmax_causal_with_its_dropout(ctx):
+    """The causal softmax kernel writing dropout(P) as a second output: the
+    same masks as the elementwise dropout (bit for bit) and the same values."""
+    s = rnd([2, 3, 200, 200], 66, -4, 4)
+    seed = np.array(11, np.int32)
+
+    run(ctx, lambda: tg.dropout(tg.softmaxCausal(T("s", [2, 3, 200, 200])), 0.25), {"s": s, "__prngSeed": seed})
+
+
 def test_layernorm_row_post_ops(ctx):
     """Row-reduction kernels that also evaluate the per-row values after the
     sum (eps, sqrt) and write them: LayerNorm forward and a row-term use of

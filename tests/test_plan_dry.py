@@ -175,3 +175,12 @@ def test_row_values_after_a_row_reduction_run_in_its_kernel():
     k = BK.plan_dry(_program(g, {}, [], g.outputs[0], None, len(g.ops)))["launches"]
     assert any(x.startswith("fused_red|mean_last") and "post:add_scalar+sqrt" in x for x in k)
     assert not any(x.startswith("fused_ew|add_scalar+sqrt") for x in k)
+
+
+def test_attention_dropout_is_written_by_the_softmax():
+    k = kinds(plan("c4"))
+    assert k.count("softmax_causal_last+dropout") == TINY["c4"]["layers"]
+    assert "softmax_causal_last" not in k
+
+    g = trace_fn(lambda: tg.dropout(tg.softmaxCausal(T("s", [2, 3, 40, 40])), 0.25))
+    assert kinds(BK.plan_dry(_program(g, {}, [], g.outputs[0], None, len(g.ops)))) == ["softmax_causal_last+dropout"]
