@@ -674,7 +674,7 @@ int gemm_tc_splits(int64_t M, int64_t N, int64_t K, int64_t batch) {
   const int64_t nk = (K + TC_BK - 1) / TC_BK;
   const int64_t sms = device_sm_count();
   if (tiles >= sms || nk < 16) return 1;
-  int64_t s = (2 * sms) / tiles;        // about two CTAs per SM
+  int64_t s = sms / tiles;              // about one unit per SM
   s = s < nk / 8 ? s : nk / 8;          // at least 8 K-stages per split
   s = s < 128 ? s : 128;                // few-tile, long-K problems (weight gradients) fill the SMs
   return s < 2 ? 1 : (int)s;
