@@ -165,7 +165,9 @@ class Graph {
   void plan_storage();
   void plan_fusion();
   void emit_launches();
-  EwInput ew_input(int t, const std::vector<int64_t>& oshape, bool& vec_ok);
+  // How an elementwise kernel of output shape oshape reads tensor t. Without
+  // with_ptr (planning, before storage exists) only the mode is decided.
+  EwInput ew_input(int t, const std::vector<int64_t>& oshape, bool& vec_ok, bool with_ptr = true);
   void emit_ew_group(int group, const int* seed_ptr, float* scratch, size_t scratch_floats,
                      const std::function<void(const std::string&, std::function<void(cudaStream_t)>)>& add);
   bool ew_internal(int t) const;
@@ -213,6 +215,11 @@ class Graph {
     // (their ops merged, ascending); each post root's output is written too.
     std::vector<int> post;
     std::vector<int> post_roots;
+    // Row reductions only: a group over the reduction's input shape that reads
+    // its per-row results, evaluated by the row's warp after them (ops
+    // ascending); epi_root's output is written.
+    std::vector<int> epi;
+    int epi_root = -1;
   };
   std::vector<EwGroup> ew_groups_;
   std::vector<int> ew_group_;        // per op: group index when the op roots a group, else -1

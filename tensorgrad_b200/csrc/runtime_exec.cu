@@ -257,6 +257,15 @@ void Graph::plan_storage() {
         if (def[r] < 0 || i < def[r]) def[r] = i;
         end[r] = std::max(end[r], i);
       }
+      if (G.epi_root >= 0) {  // and the epilogue group's result
+        const int r = views_[P.out[G.epi_root]].root;
+        used[r] = 1;
+        if (def[r] < 0 || i < def[r]) def[r] = i;
+        end[r] = std::max(end[r], i);
+        for (int m : G.epi)
+          for (int t : P.op_inputs[m])
+            if (!ew_internal(t)) touch(t, i);
+      }
       if (!G.post_roots.empty()) {
         for (int m : G.post)
           for (int t : P.op_inputs[m])
@@ -476,7 +485,7 @@ struct EwBuilder {
 
 static bool aligned16(const void* p) { return ((uintptr_t)p & 15) == 0; }
 
-EwInput Graph::ew_input(int t, const std::vector<int64_t>& oshape, bool& vec_ok) {
+EwInput Graph::ew_input(int t, const std::vector<int64_t>& oshape, bool& vec_ok, bool with_ptr) {
   EwInput in{};
   const TView& v = views_[t];
   const auto& ts = P.T[t].shape;
@@ -485,11 +494,11 @@ EwInput Graph::ew_input(int t, const std::vector<int64_t>& oshape, bool& vec_ok)
   if (v.onehot) {
     if (ts != oshape) throw TgError("Error", "internal: virtual one-hot read with broadcast");
     in.mode = IN_ONEHOT;
-    in.ptr = ptr(v.onehot_idx);
+    in.ptr = with_ptr ? ptr(v.onehot_idx) : nullptr;
     in.period = ts.back();
     return in;
   }
-  in.ptr = ptr(t);
+  in.ptr = with_ptr ? ptr(t) : nullptr;
   if (P.T[t].numel == 1) { in.mode = IN_SCALAR; return in; }
   std::vector<int64_t> pt(R, 1);
   for (size_t i = 0; i < ts.size(); ++i) pt[rd + i] = ts[i];

@@ -308,6 +308,58 @@ void Graph::plan_fusion() {
     R.post.assign(post.begin(), post.end());
   }
 
+  // Epilogue groups: a group over the row reduction's input shape that reads
+  // the reduction's per-row results (or its post ops'), and otherwise only
+  // tensors stored before the reduction in plain index modes, is evaluated by
+  // the row's warp right after the row values: one launch and one pass over
+  // the rows less (LayerNorm's normalisation, its gradient's dx).
+  for (size_t ri = 0; ri < ew_groups_.size(); ++ri) {
+    EwGroup& R = ew_groups_[ri];
+    if (R.red < 0 || R.epi_root >= 0) continue;
+    int64_t rows = 0, len = 0;
+    if (red_shape(P, R.red, &rows, &len) != RED_ROW) continue;
+    const int t = P.out[R.red];
+    if (P.T[t].numel != rows) continue;
+    const auto& vshape = P.T[P.op(R.red)["a"].i32()].shape;
+    std::set<int> rowvals = {t};
+    for (int pr : R.post_roots) rowvals.insert(P.out[pr]);
+    bool done_r = false;
+    for (int rv : rowvals) {
+      for (int c : P.consumers[rv]) {
+        auto it = owners.find(c);
+        if (it == owners.end()) continue;
+        for (int ci : it->second) {
+          EwGroup& C = ew_groups_[ci];
+          if (ci == (int)ri || C.red >= 0 || C.root < 0 || ew_group_[C.root] != ci) continue;
+          if (P.T[P.out[C.root]].shape != vshape || side(C.root) != side(R.red)) continue;
+          if ((int)C.members.size() > kMaxGroupOps) continue;
+          const std::set<int> cm(C.members.begin(), C.members.end());
+          bool ok = true;
+          for (int m : C.members)
+            for (int x : ew_operands(P, m)) {
+              if (rowvals.count(x) || cm.count(P.producer[x])) continue;
+              const TView& vx = views_[x];
+              if (vx.onehot || ew_internal(x) || P.producer[x] >= R.red) { ok = false; continue; }
+              bool dummy = true;
+              const int mode = ew_input(x, vshape, dummy, false).mode;
+              if (mode != IN_FULL && mode != IN_SCALAR && mode != IN_PERIOD && mode != IN_ROWDIV) ok = false;
+            }
+          if (!ok) continue;
+          R.epi = C.members;
+          R.epi_root = C.root;
+          ew_absorbed_[C.root] = 1;
+          ew_post_[C.root] = 1;
+          ew_group_[C.root] = -1;
+          C.root = -1;
+          done_r = true;
+          break;
+        }
+        if (done_r) break;
+      }
+      if (done_r) break;
+    }
+  }
+
   // A dropout that is the only member of its group and reads a causal
   // softmax's result is written by the softmax kernel as a second output
   // (attention's dropout on the probabilities): one read of the [.., T, T]
@@ -495,8 +547,9 @@ void Graph::emit_ew_group(int gi, const int* seed_ptr, float* scratch, size_t sc
 
   // Post ops (row reductions): evaluated by lane 0 on the row's result; their
   // other inputs are per-row tensors (read at the row) or scalars.
-  std::ostringstream post;
+  std::ostringstream post, post_w, epi;
   const bool has_post = rs == RED_ROW && !G.post_roots.empty();
+  const bool has_epi = rs == RED_ROW && G.epi_root >= 0;
   if (has_post) {
     const int t = P.out[G.red];
     const std::set<int> pm(G.post.begin(), G.post.end());
@@ -521,9 +574,42 @@ void Graph::emit_ew_group(int gi, const int* seed_ptr, float* scratch, size_t sc
       post << "      const float v" << P.out[m] << " = " << ew_expr(P, m, a, int_cmp) << ";\n";
     }
     for (size_t pr = 0; pr < G.post_roots.size(); ++pr)
-      post << "      out" << 2 + pr << "[r] = v" << P.out[G.post_roots[pr]] << ";\n";
+      post_w << "      out" << 2 + pr << "[r] = v" << P.out[G.post_roots[pr]] << ";\n";
     label += "+post:";
     for (int m : G.post) label += P.kind[m] + (m == G.post.back() ? "" : "+");
+  }
+  if (has_epi) {
+    std::set<int> rowvals = {P.out[G.red]};
+    for (int pr : G.post_roots) rowvals.insert(P.out[pr]);
+    const std::set<int> em(G.epi.begin(), G.epi.end());
+    std::map<int, int> eslot;
+    for (int m : G.epi) {
+      std::vector<std::string> a;
+      for (int x : ew_operands(P, m)) {
+        if (rowvals.count(x) || em.count(P.producer[x])) { a.push_back("v" + std::to_string(x)); continue; }
+        auto it = eslot.find(x);
+        if (it == eslot.end()) {
+          bool dummy = true;
+          EwInput in = ew_input(x, os, dummy);
+          it = eslot.emplace(x, (int)ins.size()).first;
+          ins.push_back(in);
+          const std::string pp = "p" + std::to_string(it->second), per = std::to_string(in.period) + "ll";
+          std::string ld;
+          if (in.mode == IN_FULL) ld = "__ldg(" + pp + " + e)";
+          else if (in.mode == IN_SCALAR) ld = "__ldg(" + pp + ")";
+          else if (in.mode == IN_PERIOD) ld = "__ldg(" + pp + " + e % " + per + ")";
+          else ld = "__ldg(" + pp + " + e / " + per + ")";
+          epi << "        const float z" << it->second << " = " << ld << ";\n";
+        }
+        a.push_back("z" + std::to_string(it->second));
+      }
+      if (P.kind[m] == "dropout") has_drop = true;
+      const bool int_cmp = (P.kind[m] == "less" || P.kind[m] == "greater") && P.T[ew_operands(P, m)[0]].dtype != F32;
+      epi << "        const float v" << P.out[m] << " = " << ew_expr(P, m, a, int_cmp) << ";\n";
+    }
+    epi << "        oute[e] = v" << P.out[G.epi_root] << ";\n";
+    label += "+epi:";
+    for (int m : G.epi) label += P.kind[m] + (m == G.epi.back() ? "" : "+");
   }
 
   std::ostringstream k;
@@ -532,6 +618,7 @@ void Graph::emit_ew_group(int gi, const int* seed_ptr, float* scratch, size_t sc
   k << "float* __restrict__ out, ";
   if (has_post)
     for (size_t pr = 0; pr < G.post_roots.size(); ++pr) k << "float* __restrict__ out" << 2 + pr << ", ";
+  if (has_epi) k << "float* __restrict__ oute, ";
   k << "const int* __restrict__ seedp, i64 drop_off) {\n";
   k << "  const u32 seed = " << (has_drop ? "seedp ? (u32)(*seedp) : 0u" : "0u") << ";\n";
   k << "  (void)seed; (void)drop_off;\n";
@@ -548,9 +635,15 @@ void Graph::emit_ew_group(int gi, const int* seed_ptr, float* scratch, size_t sc
     k << lane.str() << ops.str() << "      acc += " << value << ";\n    }\n";
     k << "    for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);\n";
     const std::string red = mean ? "__fdiv_rn(acc, " + lit((float)len) + ")" : "acc";
-    if (has_post) {
-      k << "    if (lane == 0) {\n      const float v" << P.out[G.red] << " = " << red << ";\n      out[r] = v"
-        << P.out[G.red] << ";\n" << post.str() << "    }\n  }\n}\n";
+    if (has_post || has_epi) {
+      // every lane holds the row sum (xor tree): the row values are computed
+      // on all lanes, lane 0 stores them, the epilogue runs over the row
+      k << "    {\n      const float v" << P.out[G.red] << " = " << red << ";\n" << post.str();
+      k << "      if (lane == 0) {\n        out[r] = v" << P.out[G.red] << ";\n" << post_w.str() << "      }\n";
+      if (has_epi)
+        k << "      for (i64 j = lane; j < " << L << "; j += 32) {\n        const i64 e = r * " << L << " + j;\n"
+          << epi.str() << "      }\n";
+      k << "    }\n  }\n}\n";
     } else {
       k << "    if (lane == 0) out[r] = " << red << ";\n  }\n}\n";
     }
@@ -618,6 +711,7 @@ void Graph::emit_ew_group(int gi, const int* seed_ptr, float* scratch, size_t sc
   for (auto& in : ins) A->in.push_back(in.ptr);
   if (has_post)
     for (int pr : G.post_roots) A->outs.push_back(ptr(P.out[pr]));
+  if (has_epi) A->outs.push_back(ptr(P.out[G.epi_root]));
   A->out = (rs == RED_COL && nchunk > 1) ? static_cast<void*>(scratch) : out;
   A->seed = seed_ptr;
   A->drop_off = (long long)ctx->rank * n;
