@@ -104,6 +104,9 @@ __global__ void __launch_bounds__(256) row_block_kernel(const float* __restrict_
   __shared__ float sm_b[8];
   __shared__ int sm_i[8];
   int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+  // rows of whole float4s from a 16-byte aligned base (log-softmax over a vocabulary)
+  const bool vec4 = KIND == ROW_LOGSOFTMAX && (D & 3) == 0 && !(reinterpret_cast<uintptr_t>(x) & 15) &&
+                    !(reinterpret_cast<uintptr_t>(out) & 15);
   for (int64_t r = blockIdx.x; r < rows; r += gridDim.x) {
     const float* xr = x + r * D;
     if (KIND == ROW_SUM || KIND == ROW_MEAN) {
@@ -140,7 +143,20 @@ __global__ void __launch_bounds__(256) row_block_kernel(const float* __restrict_
     } else {
       int64_t lim = (KIND == ROW_SOFTMAX_CAUSAL) ? (r % D) + 1 : D;
       float m = -INFINITY, s = 0.f;
-      for (int64_t j = threadIdx.x; j < lim; j += blockDim.x) {
+      int64_t j0 = 0;
+      if (vec4) {
+        // four elements per step: one rescale per float4, then their exps
+        const int64_t n4 = lim >> 2;
+        const float4* x4 = reinterpret_cast<const float4*>(xr);
+        for (int64_t q = threadIdx.x; q < n4; q += blockDim.x) {
+          const float4 v = __ldg(x4 + q);
+          const float lm = fmaxf(fmaxf(v.x, v.y), fmaxf(v.z, v.w));
+          if (lm > m) { s = (m == -INFINITY) ? 0.f : s * expf(m - lm); m = lm; }
+          s += expf(v.x - m) + expf(v.y - m) + expf(v.z - m) + expf(v.w - m);
+        }
+        j0 = n4 << 2;
+      }
+      for (int64_t j = j0 + threadIdx.x; j < lim; j += blockDim.x) {
         float v = xr[j];
         if (v > m) { s = (m == -INFINITY) ? 0.f : s * expf(m - v); m = v; }
         s += expf(v - m);
@@ -160,7 +176,16 @@ __global__ void __launch_bounds__(256) row_block_kernel(const float* __restrict_
       float* o = reinterpret_cast<float*>(out) + r * D;
       if (KIND == ROW_LOGSOFTMAX) {
         float lz = m + logf(s);
-        for (int64_t j = threadIdx.x; j < D; j += blockDim.x) o[j] = xr[j] - lz;
+        if (vec4) {
+          const float4* x4 = reinterpret_cast<const float4*>(xr);
+          float4* o4 = reinterpret_cast<float4*>(o);
+          for (int64_t q = threadIdx.x; q < (D >> 2); q += blockDim.x) {
+            const float4 v = __ldg(x4 + q);
+            o4[q] = make_float4(v.x - lz, v.y - lz, v.z - lz, v.w - lz);
+          }
+        } else {
+          for (int64_t j = threadIdx.x; j < D; j += blockDim.x) o[j] = xr[j] - lz;
+        }
       } else {
         for (int64_t j = threadIdx.x; j < D; j += blockDim.x) o[j] = j < lim ? __fdiv_rn(expf(xr[j] - m), s) : 0.f;
       }

@@ -123,6 +123,11 @@ def test_softmaxes(ctx):
     run(ctx, lambda: tg.softmax(T("a", [2, 3, 40, 40]), 2), {"a": a})
     w = rnd([4, 3000], 14, -4, 4)
     run(ctx, lambda: tg.logSoftmax(T("a", [4, 3000])), {"a": w})
+    # the C5 vocabulary (float4 rows) and an odd width (scalar rows)
+    v = rnd([3, 50304], 67, -8, 8)
+    run(ctx, lambda: tg.logSoftmax(T("a", [3, 50304])), {"a": v})
+    u = rnd([2, 4099], 68, -8, 8)
+    run(ctx, lambda: tg.logSoftmax(T("a", [2, 4099])), {"a": u})
     s = rnd([2, 2100, 2100], 15, -2, 2)
     run(ctx, lambda: tg.softmaxCausal(T("a", [2, 2100, 2100])), {"a": s})
 
