@@ -237,6 +237,14 @@ void Graph::plan_storage() {
       if (def[r] < 0 || i < def[r]) def[r] = i;
       end[r] = std::max(end[r], i);
     }
+    if (action_[i] == 102) {  // pick: reads x and the one-hot's indices
+      const int m = P.producer[P.op(i)["a"].i32()];
+      for (const char* f : {"a", "b"}) {
+        const int t = P.op(m)[f].i32();
+        touch(views_[t].onehot ? P.op(P.producer[t])["indices"].i32() : t, i);
+      }
+      continue;
+    }
     if (action_[i] == 100 || action_[i] == 101) {
       int a = P.op(i)["a"].i32();
       int oh = action_[i] == 100 ? a : P.op(P.producer[P.op(P.producer[a])["a"].i32()])["a"].i32();
@@ -650,6 +658,18 @@ void Graph::emit_launches() {
         ap.ds_ld = ap.T;
         add(label, [ap](cudaStream_t s) { launch_attn_bwd(ap, s); });
       }
+      continue;
+    }
+    if (action_[i] == 102) {
+      const int m = P.producer[O["a"].i32()];
+      int x = P.op(m)["a"].i32(), oh = P.op(m)["b"].i32();
+      if (!views_[oh].onehot) std::swap(x, oh);
+      const int idx = P.op(P.producer[oh])["indices"].i32();
+      const int64_t V = P.T[x].shape.back(), rows = P.T[o].numel;
+      const float* xp = reinterpret_cast<const float*>(ptr(x));
+      const int* ip = reinterpret_cast<const int*>(ptr(idx));
+      float* op = reinterpret_cast<float*>(ptr(o));
+      add("pick", [=](cudaStream_t s) { launch_pick(xp, ip, op, rows, V, s); });
       continue;
     }
     if (action_[i] == 100) {

@@ -107,6 +107,9 @@ namespace {
 // How a reduction consumes its input: along the last axis (rows) or the
 // leading axes (columns), or neither (not fused).
 enum RedShape { RED_NONE = 0, RED_ROW, RED_COL };
+// Rows up to this length are reduced by one warp each (and may carry post
+// ops and an epilogue); longer rows by one 256-thread block each.
+constexpr int64_t kWarpRowMax = 4096;
 RedShape red_shape(const Program& P, int r, int64_t* rows, int64_t* len) {
   const std::string& k = P.kind[r];
   if (k != "sum_last" && k != "mean_last" && k != "sum_to_shape") return RED_NONE;
@@ -117,7 +120,7 @@ RedShape red_shape(const Program& P, int r, int64_t* rows, int64_t* len) {
   if (k == "sum_last" || k == "mean_last") {
     *len = is.empty() ? 1 : is.back();
     *rows = n / std::max<int64_t>(*len, 1);
-    return *len <= 4096 ? RED_ROW : RED_NONE;
+    return RED_ROW;
   }
   if (k != "sum_to_shape") return RED_NONE;
   const auto& os = P.T[P.out[r]].shape;
@@ -131,7 +134,7 @@ RedShape red_shape(const Program& P, int r, int64_t* rows, int64_t* len) {
     else { seen_keep = true; if (seen_red) prefix = false; }
   }
   if (on == n) return RED_NONE;  // nothing reduced (a view or a copy)
-  if (prefix && !suffix) { *rows = on; *len = n / on; return *len <= 4096 ? RED_ROW : RED_NONE; }
+  if (prefix && !suffix) { *rows = on; *len = n / on; return RED_ROW; }
   if (suffix && !prefix) { *rows = n / on; *len = on; return RED_COL; }
   return RED_NONE;
 }
@@ -272,7 +275,7 @@ void Graph::plan_fusion() {
     EwGroup& R = ew_groups_[ri];
     if (R.red < 0) continue;
     int64_t rows = 0, len = 0;
-    if (red_shape(P, R.red, &rows, &len) != RED_ROW) continue;
+    if (red_shape(P, R.red, &rows, &len) != RED_ROW || len > kWarpRowMax) continue;
     const int t = P.out[R.red];
     if (P.T[t].numel != rows || !views_[t].contiguous || views_[t].onehot) continue;
     std::set<int> post(R.post.begin(), R.post.end());
@@ -317,7 +320,7 @@ void Graph::plan_fusion() {
     EwGroup& R = ew_groups_[ri];
     if (R.red < 0 || R.epi_root >= 0) continue;
     int64_t rows = 0, len = 0;
-    if (red_shape(P, R.red, &rows, &len) != RED_ROW) continue;
+    if (red_shape(P, R.red, &rows, &len) != RED_ROW || len > kWarpRowMax) continue;
     const int t = P.out[R.red];
     if (P.T[t].numel != rows) continue;
     const auto& vshape = P.T[P.op(R.red)["a"].i32()].shape;
@@ -624,7 +627,20 @@ void Graph::emit_ew_group(int gi, const int* seed_ptr, float* scratch, size_t sc
   k << "  (void)seed; (void)drop_off;\n";
   int64_t nchunk = 1;
   const std::string L = std::to_string(len) + "ll";
-  if (rs == RED_ROW) {
+  if (rs == RED_ROW && len > kWarpRowMax) {
+    // one block per row: thread t sums j = t, t + 256, ..., then warp trees and
+    // the 8 warp sums in order (a fixed order, so deterministic)
+    const bool mean = P.kind[G.red] == "mean_last";
+    k << "  __shared__ float wsum[8];\n  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;\n";
+    k << "  for (i64 r = blockIdx.x; r < " << rows << "ll; r += gridDim.x) {\n";
+    k << "    float acc = 0.f;\n#pragma unroll 4\n    for (i64 j = threadIdx.x; j < " << L << "; j += 256) {\n      const i64 e = r * "
+      << L << " + j;\n";
+    k << lane.str() << ops.str() << "      acc += " << value << ";\n    }\n";
+    k << "    for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);\n";
+    k << "    if (lane == 0) wsum[wid] = acc;\n    __syncthreads();\n";
+    k << "    if (threadIdx.x == 0) {\n      float t = 0.f;\n      for (int w = 0; w < 8; ++w) t += wsum[w];\n";
+    k << "      out[r] = " << (mean ? "__fdiv_rn(t, " + lit((float)len) + ")" : "t") << ";\n    }\n    __syncthreads();\n  }\n}\n";
+  } else if (rs == RED_ROW) {
     // one warp per row; lanes sum j = lane, lane + 32, ... then a shuffle tree
     // (the unfused row kernel's order)
     const bool mean = P.kind[G.red] == "mean_last";
@@ -718,7 +734,9 @@ void Graph::emit_ew_group(int gi, const int* seed_ptr, float* scratch, size_t sc
   const int64_t sms = device_sm_count();
   unsigned gx = 1, gy = 1;
   int tpb = 256;
-  if (rs == RED_ROW) {
+  if (rs == RED_ROW && len > kWarpRowMax) {
+    gx = (unsigned)std::max<int64_t>(1, std::min<int64_t>(rows, sms * 8));
+  } else if (rs == RED_ROW) {
     const int64_t blocks = (rows + 7) / 8;
     gx = (unsigned)std::max<int64_t>(1, std::min(blocks, sms * 16));
   } else if (rs == RED_COL) {

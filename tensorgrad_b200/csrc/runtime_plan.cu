@@ -169,6 +169,22 @@ void Graph::plan_views() {
     }
   }
 
+  // sum_last(mul(x, oneHot(idx))) over a log-softmax x (the cross-entropy
+  // gather): the row has one nonzero term, every other is x * 0 = 0 for the
+  // finite x a log-softmax gives, so the sum is x[r, idx[r]] (0 when idx is
+  // out of range), read directly instead of multiplying and summing the row.
+  for (int r = 0; r < nO; ++r) {
+    if (op_done_[r] || action_[r] != 0 || P.kind[r] != "sum_last") continue;
+    const int a = P.op(r)["a"].i32(), m = P.producer[a];
+    if (m < 0 || P.kind[m] != "mul" || op_done_[m] || pinned.count(a) || P.consumers[a].size() != 1) continue;
+    int x = P.op(m)["a"].i32(), oh = P.op(m)["b"].i32();
+    if (!views_[oh].onehot) std::swap(x, oh);
+    if (!views_[oh].onehot || views_[x].onehot || !views_[x].contiguous) continue;
+    if (P.T[x].shape != P.T[oh].shape || P.producer[x] < 0 || P.kind[P.producer[x]] != "log_softmax_last") continue;
+    action_[r] = 102;
+    op_done_[m] = 1;
+  }
+
   // A permute is a view when everything that reads it takes strided operands:
   // GEMMs, or permutes that are views themselves (decided back to front).
   std::vector<char> pview(nO, 0);

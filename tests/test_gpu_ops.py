@@ -283,6 +283,16 @@ def test_randn_and_categorical(ctx):
     run(ctx, lambda: tg.categorical(T("l", [16, 50])), {"l": logits, "__prngSeed": seed}, exact=True)
 
 
+def test_fused_long_row_reduction(ctx):
+    """A row reduction fused with its elementwise producer over rows longer
+    than a warp handles (one block per row), as the C5 loss's
+    sum(logSoftmax * oneHot)."""
+    x = rnd([5, 50304], 69, -3, 3)
+    y = rnd([5, 50304], 70)
+    run(ctx, lambda: tg.sum(tg.mul(T("x", [5, 50304]), T("y", [5, 50304])), -1), {"x": x, "y": y})
+    run(ctx, lambda: tg.mean(tg.exp(T("x", [5, 50304])), -1), {"x": x})
+
+
 def test_fused_reductions_and_shared_producers(ctx):
     """Elementwise groups consumed by row and column reductions, and a cheap
     producer recomputed by each of its consumers (the LayerNorm shapes)."""

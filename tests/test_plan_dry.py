@@ -184,3 +184,15 @@ def test_attention_dropout_is_written_by_the_softmax():
 
     g = trace_fn(lambda: tg.dropout(tg.softmaxCausal(T("s", [2, 3, 40, 40])), 0.25))
     assert kinds(BK.plan_dry(_program(g, {}, [], g.outputs[0], None, len(g.ops)))) == ["softmax_causal_last+dropout"]
+
+
+def test_long_row_reduction_consumes_its_producer():
+    g = trace_fn(lambda: tg.sum(tg.mul(T("x", [4, 50304]), T("y", [50304])), -1))
+    assert BK.plan_dry(_program(g, {}, [], g.outputs[0], None, len(g.ops)))["launches"] == ["fused_red|sum_last:mul"]
+
+
+def test_cross_entropy_gathers_the_target_log_probability():
+    """sum(logSoftmax(z) * oneHot(t)) reads one element per row (pick)."""
+    k = kinds(plan("c4"))
+    assert "pick" in k
+    assert not any(x.startswith("fused_red|sum_last:mul") for x in plan("c4")["launches"])
