@@ -202,6 +202,8 @@ void launch_gather_rows(const int* idx, const float* table, float* out, int64_t 
 size_t embedding_grad_scratch_ints(int64_t rows, int64_t V);
 void launch_embedding_grad(const int* idx, const float* dy, float* dtable, int64_t rows, int64_t V,
                            int64_t D, int* scratch, cudaStream_t s);
+// out[r] = g[r] where 0 <= t[r] < V, else 0 (the row sum of g[r] * oneHot(t)[r])
+void launch_row_hit(const float* g, const int* t, float* out, int64_t rows, int64_t V, cudaStream_t s);
 // Row pick: out[r] = x[r, t[r]] (0 if out of range)
 void launch_pick(const float* x, const int* t, float* out, int64_t rows, int64_t V, cudaStream_t s);
 

@@ -262,6 +262,18 @@ void launch_pick(const float* x, const int* t, float* out, int64_t rows, int64_t
   pick_kernel<<<(unsigned)((rows + 255) / 256), 256, 0, s>>>(x, t, out, rows, V);
 }
 
+// out[r] = g[r] where 0 <= t[r] < V, else 0: the row sum of g[r] * oneHot(t)[r].
+__global__ void row_hit_kernel(const float* __restrict__ g, const int* __restrict__ t, float* __restrict__ out,
+                               int64_t rows, int64_t V) {
+  const int64_t r = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (r >= rows) return;
+  const int k = t[r];
+  out[r] = (k >= 0 && k < V) ? g[r] : 0.f;
+}
+void launch_row_hit(const float* g, const int* t, float* out, int64_t rows, int64_t V, cudaStream_t s) {
+  row_hit_kernel<<<(unsigned)((rows + 255) / 256), 256, 0, s>>>(g, t, out, rows, V);
+}
+
 // ------------------------------------------------------------- conv / pool --
 // Max pool with the reference's scan order and strict '>' from -3.4e38, so
 // the first maximum wins (test/_eval.ts:716-738).

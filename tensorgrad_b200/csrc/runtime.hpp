@@ -202,6 +202,8 @@ class Graph {
   std::map<int, std::pair<std::vector<int>, std::vector<int>>> fused_io_;  // op -> (reads, writes) for liveness
   std::map<int, int64_t> bytes_override_;              // root -> bytes, for holders smaller than their tensor
   std::map<int, int> softmax_drop_;                    // softmax_causal op -> dropout op it also evaluates
+  std::set<std::pair<int, int>> no_read_;              // (op, tensor): the op's result is formed without reading it
+  std::vector<int> eff_consumers(int t) const;         // consumers of t that read it
   std::map<int, std::vector<int>> extra_writes_;       // op -> further tensors its launch writes
   void plan_attention(const std::set<int>& observable);
   // Fused elementwise groups. A group is rooted at the op whose output it

@@ -237,6 +237,19 @@ void Graph::plan_storage() {
       if (def[r] < 0 || i < def[r]) def[r] = i;
       end[r] = std::max(end[r], i);
     }
+    if (action_[i] == 103) {  // row hit: reads g and the one-hot's indices
+      const int m = P.producer[P.op(i)["a"].i32()];
+      for (const char* f : {"a", "b"}) {
+        const int t = P.op(m)[f].i32();
+        touch(views_[t].onehot ? P.op(P.producer[t])["indices"].i32() : P.op(P.producer[t])["a"].i32(), i);
+      }
+      int o = P.out[i];
+      const int r = views_[o].root;
+      used[r] = 1;
+      if (def[r] < 0 || i < def[r]) def[r] = i;
+      end[r] = std::max(end[r], i);
+      continue;
+    }
     if (action_[i] == 102) {  // pick: reads x and the one-hot's indices
       const int m = P.producer[P.op(i)["a"].i32()];
       for (const char* f : {"a", "b"}) {
@@ -658,6 +671,18 @@ void Graph::emit_launches() {
         ap.ds_ld = ap.T;
         add(label, [ap](cudaStream_t s) { launch_attn_bwd(ap, s); });
       }
+      continue;
+    }
+    if (action_[i] == 103) {
+      const int m = P.producer[O["a"].i32()];
+      int u = P.op(m)["a"].i32(), oh = P.op(m)["b"].i32();
+      if (!views_[oh].onehot) std::swap(u, oh);
+      const int idx = P.op(P.producer[oh])["indices"].i32(), g = P.op(P.producer[u])["a"].i32();
+      const int64_t V = P.T[oh].shape.back(), rows = P.T[o].numel;
+      const float* gp = reinterpret_cast<const float*>(ptr(g));
+      const int* ip = reinterpret_cast<const int*>(ptr(idx));
+      float* op = reinterpret_cast<float*>(ptr(o));
+      add("row_hit", [=](cudaStream_t s) { launch_row_hit(gp, ip, op, rows, V, s); });
       continue;
     }
     if (action_[i] == 102) {

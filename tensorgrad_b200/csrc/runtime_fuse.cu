@@ -209,7 +209,7 @@ void Graph::plan_fusion() {
         for (int m : mem[p]) costly = costly || expensive_kind(P.kind[m]);
         if (costly) continue;
       }
-      const auto& cs = P.consumers[t];
+      const std::vector<int> cs = eff_consumers(t);
       if (cs.size() == 1) {
         // sole consumer: the producer's group moves into this one
         if (merge_into(i, p, t)) { root[p] = 0; ext[p].clear(); }
@@ -230,7 +230,7 @@ void Graph::plan_fusion() {
   }
   // Producers whose every consumer evaluates them in place are not stored.
   for (int p = 0; p < nO; ++p)
-    if (root[p] && copied[P.out[p]] > 0 && copied[P.out[p]] == (int)P.consumers[P.out[p]].size()) root[p] = 0;
+    if (root[p] && copied[P.out[p]] > 0 && copied[P.out[p]] == (int)eff_consumers(P.out[p]).size()) root[p] = 0;
 
   // A reduction over the output of a group it alone consumes evaluates the
   // group per element instead of reading it back.
@@ -241,7 +241,7 @@ void Graph::plan_fusion() {
     if (red_shape(P, r, &rows, &len) == RED_NONE) continue;
     const int t = P.op(r)["a"].i32(), p = P.producer[t];
     if (p < 0 || !root[p] || !inlinable(t) || side(p) != side(r)) continue;
-    if (P.consumers[t].size() != 1 || (int)ext[p].size() > kMaxGroupInputs) continue;
+    if (eff_consumers(t).size() != 1 || (int)ext[p].size() > kMaxGroupInputs) continue;
     red_of[p] = r;
   }
 

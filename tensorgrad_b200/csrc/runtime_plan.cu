@@ -185,6 +185,26 @@ void Graph::plan_views() {
     op_done_[m] = 1;
   }
 
+  // sum_last(mul(broadcast_to(g), oneHot(idx))) with g one value per row (the
+  // cross-entropy gradient's one-hot term): the row sum is g[r] when idx[r] is
+  // in range, else 0, formed without reading the [rows, V] product, which is
+  // then left to its other consumers.
+  for (int r = 0; r < nO; ++r) {
+    if (op_done_[r] || action_[r] != 0 || P.kind[r] != "sum_last") continue;
+    const int a = P.op(r)["a"].i32(), m = P.producer[a];
+    if (m < 0 || P.kind[m] != "mul" || op_done_[m] || pinned.count(a)) continue;
+    int u = P.op(m)["a"].i32(), oh = P.op(m)["b"].i32();
+    if (!views_[oh].onehot) std::swap(u, oh);
+    if (!views_[oh].onehot || views_[u].onehot) continue;
+    const int pu = P.producer[u];
+    if (pu < 0 || P.kind[pu] != "broadcast_to" || P.T[u].shape != P.T[oh].shape) continue;
+    const int g = P.op(pu)["a"].i32();
+    if (P.T[g].numel != P.T[P.out[r]].numel || views_[g].onehot || !views_[g].contiguous) continue;
+    action_[r] = 103;
+    no_read_.insert({r, a});
+    if (P.consumers[a].size() == 1) op_done_[m] = 1;  // nothing else reads the product
+  }
+
   // A permute is a view when everything that reads it takes strided operands:
   // GEMMs, or permutes that are views themselves (decided back to front).
   std::vector<char> pview(nO, 0);
@@ -623,4 +643,13 @@ void Graph::plan_attention(const std::set<int>& observable) {
   }
 }
 
+}  // namespace tg
+
+namespace tg {
+std::vector<int> Graph::eff_consumers(int t) const {
+  std::vector<int> out;
+  for (int c : P.consumers[t])
+    if (!no_read_.count({c, t})) out.push_back(c);
+  return out;
+}
 }  // namespace tg

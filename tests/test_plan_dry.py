@@ -196,3 +196,12 @@ def test_cross_entropy_gathers_the_target_log_probability():
     k = kinds(plan("c4"))
     assert "pick" in k
     assert not any(x.startswith("fused_red|sum_last:mul") for x in plan("c4")["launches"])
+
+
+def test_cross_entropy_backward_writes_no_dense_one_hot_gradient():
+    """The backward of the gathered term, sum(broadcast(g) * oneHot(t)), becomes
+    one value per row (row_hit) that the dlogits group reads; no [rows, V]
+    one-hot gradient is written."""
+    launches = plan("c4")["launches"]
+    assert "row_hit" in kinds(plan("c4"))
+    assert "fused_ew|broadcast_to+mul" not in launches
