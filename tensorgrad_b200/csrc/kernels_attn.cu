@@ -73,15 +73,27 @@ __device__ __forceinline__ AFrag afrag_at(const float* row_g, int stride) {
   return afrag(row_g[0], row_g[8 * stride], row_g[4], row_g[8 * stride + 4]);
 }
 
-// c += a * b for one 16x8x8 step with both operands split (3xTF32: lo*hi,
-// hi*lo, hi*hi); b0, b1 are the two B values of the fragment.
-__device__ __forceinline__ void mma3(float (&c)[4], const AFrag& a, float b0, float b1) {
-  uint32_t bh0, bl0, bh1, bl1;
-  split_tf32(b0, bh0, bl0);
-  split_tf32(b1, bh1, bl1);
-  mma8(c, a.l[0], a.l[1], a.l[2], a.l[3], bh0, bh1);
-  mma8(c, a.h[0], a.h[1], a.h[2], a.h[3], bl0, bl1);
-  mma8(c, a.h[0], a.h[1], a.h[2], a.h[3], bh0, bh1);
+// c[n] += a * b_n for N independent 16x8x8 steps (n = N0 .. N0 + N - 1),
+// issued as three passes over n (lo*hi, then hi*lo, then hi*hi) so that
+// consecutive MMAs never wait on one accumulator. Both operands are split
+// (3xTF32); the dropped lo*lo term is about 2^-22 relative. ldb(n, b0, b1)
+// fetches the two B values of step n.
+template <int N0, int N, int C, class LoadB>
+__device__ __forceinline__ void mma3n(float (&c)[C][4], const AFrag& a, LoadB ldb) {
+  uint32_t bh[N][2], bl[N][2];
+#pragma unroll
+  for (int n = 0; n < N; ++n) {
+    float b0, b1;
+    ldb(N0 + n, b0, b1);
+    split_tf32(b0, bh[n][0], bl[n][0]);
+    split_tf32(b1, bh[n][1], bl[n][1]);
+  }
+#pragma unroll
+  for (int n = 0; n < N; ++n) mma8(c[N0 + n], a.l[0], a.l[1], a.l[2], a.l[3], bh[n][0], bh[n][1]);
+#pragma unroll
+  for (int n = 0; n < N; ++n) mma8(c[N0 + n], a.h[0], a.h[1], a.h[2], a.h[3], bl[n][0], bl[n][1]);
+#pragma unroll
+  for (int n = 0; n < N; ++n) mma8(c[N0 + n], a.h[0], a.h[1], a.h[2], a.h[3], bh[n][0], bh[n][1]);
 }
 
 __device__ __forceinline__ float vld(const AttnView& v, int b, int h, int t, int c) {
@@ -182,13 +194,13 @@ __global__ void __launch_bounds__(128) attn_fwd_kernel(const __grid_constant__ A
     __syncthreads();
     float s[8][4];
 #pragma unroll
-    for (int nt = 0; nt < 8; ++nt) {
-      s[nt][0] = s[nt][1] = s[nt][2] = s[nt][3] = 0.f;
+    for (int nt = 0; nt < 8; ++nt) s[nt][0] = s[nt][1] = s[nt][2] = s[nt][3] = 0.f;
 #pragma unroll
-      for (int kk = 0; kk < D / 8; ++kk) {
-        const float* kr = sK + (8 * nt + g) * SQ + 8 * kk + t;
-        mma3(s[nt], qa[kk], kr[0], kr[4]);
-      }
+    for (int kk = 0; kk < D / 8; ++kk) {
+      const float* kb8 = sK + g * SQ + 8 * kk + t;
+      const auto ldk = [&](int nt, float& b0, float& b1) { b0 = kb8[8 * nt * SQ]; b1 = kb8[8 * nt * SQ + 4]; };
+      mma3n<0, 4>(s, qa[kk], ldk);
+      mma3n<4, 4>(s, qa[kk], ldk);
     }
     // scale (in log2 units), causal/tail mask, online softmax over this key block
     const bool edge = kb == qb || kb * AB + AB > P.T;
@@ -240,11 +252,8 @@ __global__ void __launch_bounds__(128) attn_fwd_kernel(const __grid_constant__ A
 #pragma unroll 1
     for (int kk = 0; kk < 8; ++kk) {
       const AFrag pa = afrag_at(sP + g * SPP + 8 * kk + t, SPP);
-#pragma unroll
-      for (int n = 0; n < D / 8; ++n) {
-        const float* vr = sV + (8 * kk + t) * SV + 8 * n + g;
-        mma3(oacc[n], pa, vr[0], vr[4 * SV]);
-      }
+      const float* vr = sV + (8 * kk + t) * SV + g;
+      mma3n<0, D / 8>(oacc, pa, [&](int n, float& b0, float& b1) { b0 = vr[8 * n]; b1 = vr[8 * n + 4 * SV]; });
     }
     __syncwarp();
   }
@@ -330,13 +339,14 @@ __global__ void __launch_bounds__(128, 3) attn_bwd_kv_kernel(const __grid_consta
     for (int kk = 0; kk < D / 8; ++kk) {
       const AFrag ka = afrag_at(sK + (16 * w + g) * SQ + 8 * kk + t, SQ);
       const AFrag va = afrag_at(sV + (16 * w + g) * SQ + 8 * kk + t, SQ);
-#pragma unroll
-      for (int nt = 0; nt < 8; ++nt) {
-        const float* qr = sQ + (8 * nt + g) * SQ + 8 * kk + t;
-        mma3(st[nt], ka, qr[0], qr[4]);
-        const float* orr = sO + (8 * nt + g) * SQ + 8 * kk + t;
-        mma3(dp[nt], va, orr[0], orr[4]);
-      }
+      const float* qr = sQ + g * SQ + 8 * kk + t;
+      const float* orr = sO + g * SQ + 8 * kk + t;
+      const auto ldq = [&](int nt, float& b0, float& b1) { b0 = qr[8 * nt * SQ]; b1 = qr[8 * nt * SQ + 4]; };
+      const auto ldo = [&](int nt, float& b0, float& b1) { b0 = orr[8 * nt * SQ]; b1 = orr[8 * nt * SQ + 4]; };
+      mma3n<0, 4>(st, ka, ldq);
+      mma3n<0, 4>(dp, va, ldo);
+      mma3n<4, 4>(st, ka, ldq);
+      mma3n<4, 4>(dp, va, ldo);
     }
     // P^T, dropout, dS^T; Pd^T staged for dV
     const float c2 = P.scale * LOG2E;
@@ -365,11 +375,8 @@ __global__ void __launch_bounds__(128, 3) attn_bwd_kv_kernel(const __grid_consta
 #pragma unroll 1
     for (int kk = 0; kk < 8; ++kk) {
       const AFrag pa = afrag_at(sP + g * SPP + 8 * kk + t, SPP);
-#pragma unroll
-      for (int n = 0; n < D / 8; ++n) {
-        const float* orr = sO + (8 * kk + t) * SQ + 8 * n + g;
-        mma3(dv[n], pa, orr[0], orr[4 * SQ]);
-      }
+      const float* orr = sO + (8 * kk + t) * SQ + g;
+      mma3n<0, D / 8>(dv, pa, [&](int n, float& b0, float& b1) { b0 = orr[8 * n]; b1 = orr[8 * n + 4 * SQ]; });
     }
     __syncwarp();
     // dS: staged for dK and written out (queries of this block, this warp's keys)
@@ -387,11 +394,8 @@ __global__ void __launch_bounds__(128, 3) attn_bwd_kv_kernel(const __grid_consta
 #pragma unroll 1
     for (int kk = 0; kk < 8; ++kk) {
       const AFrag pa = afrag_at(sP + g * SPP + 8 * kk + t, SPP);
-#pragma unroll
-      for (int n = 0; n < D / 8; ++n) {
-        const float* qr = sQ + (8 * kk + t) * SQ + 8 * n + g;
-        mma3(dk[n], pa, qr[0], qr[4 * SQ]);
-      }
+      const float* qr = sQ + (8 * kk + t) * SQ + g;
+      mma3n<0, D / 8>(dk, pa, [&](int n, float& b0, float& b1) { b0 = qr[8 * n]; b1 = qr[8 * n + 4 * SQ]; });
     }
   }
 #pragma unroll
@@ -434,11 +438,8 @@ __global__ void __launch_bounds__(128) attn_bwd_q_kernel(const __grid_constant__
 #pragma unroll 1
     for (int kk = 0; kk < 8; ++kk) {
       const AFrag sa = afrag_at(sS + (16 * w + g) * SPP + 8 * kk + t, SPP);
-#pragma unroll
-      for (int n = 0; n < D / 8; ++n) {
-        const float* kr = sK + (8 * kk + t) * SK + 8 * n + g;
-        mma3(dq[n], sa, kr[0], kr[4 * SK]);
-      }
+      const float* kr = sK + (8 * kk + t) * SK + g;
+      mma3n<0, D / 8>(dq, sa, [&](int n, float& b0, float& b1) { b0 = kr[8 * n]; b1 = kr[8 * n + 4 * SK]; });
     }
   }
 #pragma unroll
