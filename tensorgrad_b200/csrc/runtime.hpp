@@ -224,6 +224,7 @@ class Graph {
     int epi_root = -1;
   };
   std::vector<EwGroup> ew_groups_;
+  std::map<int, int> row_values(const EwGroup& G) const;  // row value tensor -> the value it aliases
   std::vector<int> ew_group_;        // per op: group index when the op roots a group, else -1
   std::vector<char> ew_absorbed_;    // per op: value computed inside the groups that use it (no storage)
   std::vector<char> ew_post_;        // per op: absorbed as a row reduction's post op, output still stored

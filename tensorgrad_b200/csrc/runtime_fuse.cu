@@ -97,6 +97,29 @@ constexpr int kMaxGroupOps = 48;
 
 }  // namespace
 
+// A row reduction's per-row values (its result and its post ops' results),
+// each mapped to itself, plus the reshapes / stop_gradients of them that keep
+// the element count (keepDims adds a unit dimension), each mapped to the value
+// it aliases.
+std::map<int, int> Graph::row_values(const EwGroup& G) const {
+  std::map<int, int> rv = {{P.out[G.red], P.out[G.red]}};
+  for (int pr : G.post_roots) rv[P.out[pr]] = P.out[pr];
+  std::vector<int> work;
+  for (const auto& kv : rv) work.push_back(kv.first);
+  while (!work.empty()) {
+    const int x = work.back();
+    work.pop_back();
+    for (int c : P.consumers[x]) {
+      const int y = P.out[c];
+      if ((P.kind[c] == "reshape" || P.kind[c] == "stop_gradient") && P.T[y].numel == P.T[x].numel && !rv.count(y)) {
+        rv[y] = rv[x];
+        work.push_back(y);
+      }
+    }
+  }
+  return rv;
+}
+
 bool Graph::ew_internal(int t) const {
   if (ew_absorbed_.empty()) return false;
   const int p = P.producer[t];
@@ -324,8 +347,8 @@ void Graph::plan_fusion() {
     const int t = P.out[R.red];
     if (P.T[t].numel != rows) continue;
     const auto& vshape = P.T[P.op(R.red)["a"].i32()].shape;
-    std::set<int> rowvals = {t};
-    for (int pr : R.post_roots) rowvals.insert(P.out[pr]);
+    std::set<int> rowvals;
+    for (const auto& kv : row_values(R)) rowvals.insert(kv.first);
     bool done_r = false;
     for (int rv : rowvals) {
       for (int c : P.consumers[rv]) {
@@ -582,8 +605,11 @@ void Graph::emit_ew_group(int gi, const int* seed_ptr, float* scratch, size_t sc
     for (int m : G.post) label += P.kind[m] + (m == G.post.back() ? "" : "+");
   }
   if (has_epi) {
-    std::set<int> rowvals = {P.out[G.red]};
-    for (int pr : G.post_roots) rowvals.insert(P.out[pr]);
+    const std::map<int, int> rva = row_values(G);
+    std::set<int> rowvals;
+    for (const auto& kv : rva)
+      if (rowvals.insert(kv.first).second && kv.first != kv.second)
+        epi << "        const float v" << kv.first << " = v" << kv.second << ";\n";
     const std::set<int> em(G.epi.begin(), G.epi.end());
     std::map<int, int> eslot;
     for (int m : G.epi) {

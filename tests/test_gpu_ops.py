@@ -184,6 +184,21 @@ def test_layernorm_row_post_ops(ctx):
     run(ctx, build, {"x": x})
 
 
+def test_softmax_gradient_row_epilogue(ctx):
+    """The softmax gradient with dropout, P * (dropout(dP) - sum(dropout(dP) * P,
+    keepDims)): one row-reduction launch whose epilogue reads the row sum
+    through its keepDims reshape and recomputes the same dropout mask."""
+    sh = [2, 3, 200, 200]
+    dp, p = rnd(sh, 67), rnd(sh, 68, 0, 1)
+    seed = np.array(5, np.int32)
+
+    def build():
+        dP, P = T("dp", sh), T("p", sh)
+        d = tg.dropout(dP, 0.2)
+        return tg.mulScalar(tg.mul(tg.sub(d, tg.sum(tg.mul(d, P), -1, keepDims=True)), P), 0.125)
+    run(ctx, build, {"dp": dp, "p": p, "__prngSeed": seed})
+
+
 def test_sum_to_shape_middle(ctx):
     """Reduced dims on both sides of the kept ones (the conv bias gradient
     [B, C, H, W] -> [C, 1, 1]), small and at the CNN benchmark's size."""

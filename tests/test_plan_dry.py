@@ -205,3 +205,18 @@ def test_cross_entropy_backward_writes_no_dense_one_hot_gradient():
     launches = plan("c4")["launches"]
     assert "row_hit" in kinds(plan("c4"))
     assert "fused_ew|broadcast_to+mul" not in launches
+
+
+def test_row_sum_read_through_keepdims_reshape_is_an_epilogue():
+    """sum(..., keepDims) is a row sum plus a reshape; the group that reads it
+    through the reshape still runs as the reduction's epilogue (the softmax
+    gradient: one launch, not two)."""
+    sh = [4, 2, 64, 64]
+
+    def f():
+        dP, P = T("dp", sh), T("p", sh)
+        d = tg.dropout(dP, 0.2)
+        return tg.mul(tg.sub(d, tg.sum(tg.mul(d, P), -1, keepDims=True)), P)
+    g = trace_fn(f)
+    assert BK.plan_dry(_program(g, {}, [], g.outputs[0], None, len(g.ops)))["launches"] == [
+        "fused_red|sum_last:dropout+mul+epi:dropout+sub+mul"]
