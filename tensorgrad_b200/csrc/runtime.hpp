@@ -222,6 +222,11 @@ class Graph {
     // ascending); epi_root's output is written.
     std::vector<int> epi;
     int epi_root = -1;
+    // Row reductions only: a plain row reduction (mean_last / sum_last of a
+    // stored tensor over the same rows) computed by this launch as a first
+    // pass over each row; its result is a register for the rest of the
+    // kernel and is written too (LayerNorm's mean before its variance).
+    int pre = -1;
   };
   std::vector<EwGroup> ew_groups_;
   std::map<int, int> row_values(const EwGroup& G) const;  // row value tensor -> the value it aliases

@@ -278,6 +278,7 @@ void Graph::plan_storage() {
         if (def[r] < 0 || i < def[r]) def[r] = i;
         end[r] = std::max(end[r], i);
       }
+      if (G.pre >= 0) touch(P.op(G.pre)["a"].i32(), i);  // the absorbed first-pass reduction's input
       if (G.epi_root >= 0) {  // and the epilogue group's result
         const int r = views_[P.out[G.epi_root]].root;
         used[r] = 1;

@@ -120,6 +120,22 @@ std::map<int, int> Graph::row_values(const EwGroup& G) const {
   return rv;
 }
 
+// The tensors that alias value t through element-count-preserving reshapes
+// and stop_gradients (views), t included.
+static std::set<int> view_aliases(const Program& P, int t) {
+  std::set<int> s = {t};
+  std::vector<int> work = {t};
+  while (!work.empty()) {
+    const int x = work.back();
+    work.pop_back();
+    for (int c : P.consumers[x])
+      if ((P.kind[c] == "reshape" || P.kind[c] == "stop_gradient") && P.T[P.out[c]].numel == P.T[x].numel &&
+          s.insert(P.out[c]).second)
+        work.push_back(P.out[c]);
+  }
+  return s;
+}
+
 bool Graph::ew_internal(int t) const {
   if (ew_absorbed_.empty()) return false;
   const int p = P.producer[t];
@@ -411,6 +427,55 @@ void Graph::plan_fusion() {
       break;
     }
   }
+
+  // A plain row mean / sum of a stored tensor whose result a fused row
+  // reduction over the same rows reads later in the step (LayerNorm: the
+  // mean, then the variance of x - mean, then the normalisation) is computed
+  // by that reduction's kernel as a first pass over each row: one launch and
+  // one read of the mean less. Every reader of the result must run in that
+  // launch or after it, and its aliases must be views.
+  for (size_t ri = 0; ri < ew_groups_.size(); ++ri) {
+    EwGroup& R = ew_groups_[ri];
+    if (R.red < 0 || R.root < 0 || R.pre >= 0) continue;
+    int64_t rows = 0, len = 0;
+    if (red_shape(P, R.red, &rows, &len) != RED_ROW || len > kWarpRowMax) continue;
+    const auto& vshape = P.T[P.op(R.red)["a"].i32()].shape;
+    std::set<int> readers(R.members.begin(), R.members.end());
+    readers.insert(R.post.begin(), R.post.end());
+    readers.insert(R.epi.begin(), R.epi.end());
+    for (int m : R.members) {
+      for (int x : ew_operands(P, m)) {
+        int b = x;
+        while (P.producer[b] >= 0 && (P.kind[P.producer[b]] == "reshape" || P.kind[P.producer[b]] == "stop_gradient")) {
+          const int src = P.op(P.producer[b])["a"].i32();
+          if (P.T[src].numel != P.T[b].numel) break;
+          b = src;
+        }
+        const int r1 = P.producer[b];
+        if (r1 < 0 || r1 >= R.red || op_done_[r1] || action_[r1] != 0 || ew_group_of(r1) >= 0) continue;
+        if (P.kind[r1] != "mean_last" && P.kind[r1] != "sum_last") continue;
+        int64_t rows1 = 0, len1 = 0;
+        if (red_shape(P, r1, &rows1, &len1) != RED_ROW || rows1 != rows || len1 != len) continue;
+        const int a1 = P.op(r1)["a"].i32();
+        if (views_[a1].onehot || ew_internal(a1) || P.T[a1].shape != vshape) continue;
+        bool dummy = true;
+        if (ew_input(a1, vshape, dummy, false).mode != IN_FULL) continue;
+        bool ok = views_[b].root == b;
+        for (int y : view_aliases(P, b))
+          for (int c : P.consumers[y]) {
+            const bool alias = (P.kind[c] == "reshape" || P.kind[c] == "stop_gradient") &&
+                               P.T[P.out[c]].numel == P.T[y].numel;
+            if (alias ? !op_done_[c] : (!readers.count(c) && c <= R.red)) ok = false;
+          }
+        if (!ok) continue;
+        R.pre = r1;
+        op_done_[r1] = 1;
+        extra_writes_[R.red].push_back(b);
+        break;
+      }
+      if (R.pre >= 0) break;
+    }
+  }
 }
 
 namespace {
@@ -502,10 +567,17 @@ void Graph::emit_ew_group(int gi, const int* seed_ptr, float* scratch, size_t sc
   bool has_drop = false;
   std::ostringstream ops;
   std::string label;
+  // the first-pass row value (and its views), a register in the row loop
+  const std::set<int> pre_vals = G.pre >= 0 ? view_aliases(P, P.out[G.pre]) : std::set<int>{};
+  int pre_slot = -1;
+  if (G.pre >= 0) {
+    pre_slot = (int)ins.size();
+    ins.push_back(ew_input(P.op(G.pre)["a"].i32(), os, vec));
+  }
   for (int m : G.members) {
     std::vector<std::string> a;
     for (int t : ew_operands(P, m)) {
-      if (member_set.count(P.producer[t])) { a.push_back("v" + std::to_string(t)); continue; }
+      if (member_set.count(P.producer[t]) || pre_vals.count(t)) { a.push_back("v" + std::to_string(t)); continue; }
       auto it = slot_of.find(t);
       if (it == slot_of.end()) {
         it = slot_of.emplace(t, (int)ins.size()).first;
@@ -583,7 +655,7 @@ void Graph::emit_ew_group(int gi, const int* seed_ptr, float* scratch, size_t sc
     for (int m : G.post) {
       std::vector<std::string> a;
       for (int x : ew_operands(P, m)) {
-        if (x == t || pm.count(P.producer[x])) { a.push_back("v" + std::to_string(x)); continue; }
+        if (x == t || pm.count(P.producer[x]) || pre_vals.count(x)) { a.push_back("v" + std::to_string(x)); continue; }
         auto it = pslot.find(x);
         if (it == pslot.end()) {
           it = pslot.emplace(x, (int)ins.size()).first;
@@ -615,7 +687,7 @@ void Graph::emit_ew_group(int gi, const int* seed_ptr, float* scratch, size_t sc
     for (int m : G.epi) {
       std::vector<std::string> a;
       for (int x : ew_operands(P, m)) {
-        if (rowvals.count(x) || em.count(P.producer[x])) { a.push_back("v" + std::to_string(x)); continue; }
+        if (rowvals.count(x) || em.count(P.producer[x]) || pre_vals.count(x)) { a.push_back("v" + std::to_string(x)); continue; }
         auto it = eslot.find(x);
         if (it == eslot.end()) {
           bool dummy = true;
@@ -648,6 +720,7 @@ void Graph::emit_ew_group(int gi, const int* seed_ptr, float* scratch, size_t sc
   if (has_post)
     for (size_t pr = 0; pr < G.post_roots.size(); ++pr) k << "float* __restrict__ out" << 2 + pr << ", ";
   if (has_epi) k << "float* __restrict__ oute, ";
+  if (G.pre >= 0) k << "float* __restrict__ outp, ";
   k << "const int* __restrict__ seedp, i64 drop_off) {\n";
   k << "  const u32 seed = " << (has_drop ? "seedp ? (u32)(*seedp) : 0u" : "0u") << ";\n";
   k << "  (void)seed; (void)drop_off;\n";
@@ -672,6 +745,19 @@ void Graph::emit_ew_group(int gi, const int* seed_ptr, float* scratch, size_t sc
     const bool mean = P.kind[G.red] == "mean_last";
     k << "  const int lane = threadIdx.x & 31;\n  const i64 nw = ((i64)gridDim.x * 256) >> 5;\n";
     k << "  for (i64 r = (((i64)blockIdx.x * 256 + threadIdx.x) >> 5); r < " << rows << "ll; r += nw) {\n";
+    if (G.pre >= 0) {
+      // first pass: the absorbed row reduction, in the same lane order and
+      // tree as the row kernels; lane 0 stores it, every lane keeps it
+      const int b = P.out[G.pre];
+      k << "    float accp = 0.f;\n#pragma unroll 4\n    for (i64 j = lane; j < " << L << "; j += 32) accp += __ldg(p"
+        << pre_slot << " + r * " << L << " + j);\n";
+      k << "    for (int o = 16; o > 0; o >>= 1) accp += __shfl_xor_sync(0xffffffffu, accp, o);\n";
+      k << "    const float v" << b << " = "
+        << (P.kind[G.pre] == "mean_last" ? "__fdiv_rn(accp, " + lit((float)len) + ")" : "accp") << ";\n";
+      for (int y : pre_vals)
+        if (y != b) k << "    const float v" << y << " = v" << b << ";\n";
+      k << "    if (lane == 0) outp[r] = v" << b << ";\n";
+    }
     k << "    float acc = 0.f;\n#pragma unroll 4\n    for (i64 j = lane; j < " << L << "; j += 32) {\n      const i64 e = r * " << L
       << " + j;\n";
     k << lane.str() << ops.str() << "      acc += " << value << ";\n    }\n";
@@ -754,6 +840,7 @@ void Graph::emit_ew_group(int gi, const int* seed_ptr, float* scratch, size_t sc
   if (has_post)
     for (int pr : G.post_roots) A->outs.push_back(ptr(P.out[pr]));
   if (has_epi) A->outs.push_back(ptr(P.out[G.epi_root]));
+  if (G.pre >= 0) A->outs.push_back(ptr(P.out[G.pre]));
   A->out = (rs == RED_COL && nchunk > 1) ? static_cast<void*>(scratch) : out;
   A->seed = seed_ptr;
   A->drop_off = (long long)ctx->rank * n;
@@ -773,7 +860,8 @@ void Graph::emit_ew_group(int gi, const int* seed_ptr, float* scratch, size_t sc
     const int64_t blocks = (work + 255) / 256;
     gx = (unsigned)std::max<int64_t>(1, std::min(blocks, sms * 8));
   }
-  if (G.red >= 0) label = "fused_red|" + P.kind[G.red] + ":" + label.substr(0, 150);
+  if (G.red >= 0)
+    label = "fused_red|" + (G.pre >= 0 ? P.kind[G.pre] + ">" : std::string()) + P.kind[G.red] + ":" + label.substr(0, 150);
   else if (G.members.size() > 1) label = "fused_ew|" + label.substr(0, 160);
   float* fold_out = reinterpret_cast<float*>(out);
   const int64_t fold_n = (rs == RED_COL && nchunk > 1) ? nchunk : 0, fold_len = len;

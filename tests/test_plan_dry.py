@@ -220,3 +220,32 @@ def test_row_sum_read_through_keepdims_reshape_is_an_epilogue():
     g = trace_fn(f)
     assert BK.plan_dry(_program(g, {}, [], g.outputs[0], None, len(g.ops)))["launches"] == [
         "fused_red|sum_last:dropout+mul+epi:dropout+sub+mul"]
+
+
+def test_layernorm_mean_is_a_first_pass_of_the_variance_kernel():
+    """LayerNorm's mean (a plain row mean of a stored tensor) runs inside the
+    variance reduction's kernel as a first pass over each row: one launch for
+    mean, variance and normalisation."""
+    def f():
+        X = T("x", [300, 384])
+        d = tg.sub(X, tg.mean(X, -1, keepDims=True))
+        sd = tg.sqrt(tg.addScalar(tg.mean(tg.mul(d, d), -1, keepDims=True), 1e-5))
+        return tg.add(tg.div(d, sd), tg.mul(sd, sd))
+    g = trace_fn(f)
+    assert BK.plan_dry(_program(g, {}, [], g.outputs[0], None, len(g.ops)))["launches"] == [
+        "fused_red|mean_last>mean_last:sub+mul+post:add_scalar+sqrt+mul+epi:sub+div+add"]
+    assert "mean_last" not in plan("c4")["launches"]
+
+
+def test_mean_read_before_the_variance_keeps_its_own_launch():
+    """A mean that another launch reads before the variance kernel runs is not
+    moved into it."""
+    def f():
+        X = T("x", [300, 384])
+        mu = tg.mean(X, -1, keepDims=True)
+        early = tg.sum(tg.mul(mu, mu))                       # reads the mean first
+        d = tg.sub(X, mu)
+        return tg.add(tg.mean(tg.mul(d, d), -1), early)
+    g = trace_fn(f)
+    launches = BK.plan_dry(_program(g, {}, [], g.outputs[0], None, len(g.ops)))["launches"]
+    assert "mean_last" in launches
