@@ -227,9 +227,14 @@ class Graph {
     // pass over each row; its result is a register for the rest of the
     // kernel and is written too (LayerNorm's mean before its variance).
     int pre = -1;
+    // Column reductions only: the elementwise group that produced the summed
+    // tensor, whose value this launch also stores (its output has other
+    // readers). The launch runs at that group's position.
+    int wt = -1;
   };
   std::vector<EwGroup> ew_groups_;
-  std::map<int, int> row_values(const EwGroup& G) const;  // row value tensor -> the value it aliases
+  std::map<int, int> row_values(const EwGroup& G) const;
+  std::set<int> wt_reds_;           // column reductions computed by their producer group's launch  // row value tensor -> the value it aliases
   std::vector<int> ew_group_;        // per op: group index when the op roots a group, else -1
   std::vector<char> ew_absorbed_;    // per op: value computed inside the groups that use it (no storage)
   std::vector<char> ew_post_;        // per op: absorbed as a row reduction's post op, output still stored

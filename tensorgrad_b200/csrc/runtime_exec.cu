@@ -357,7 +357,7 @@ void Graph::plan_storage() {
     bool direct = R >= 0 && vg.off == 0 && vg.contiguous && P.T[R].numel == P.T[G].numel &&
                   P.producer[R] >= 0 && !is_leaf_kind(P.kind[P.producer[R]]) &&
                   !is_const_kind(P.kind[P.producer[R]]) && loc_[R].arena < 0 && !grad_placed.count(R) &&
-                  !op_done_[P.producer[R]] && !ew_is_absorbed(P.producer[R]);
+                  (!op_done_[P.producer[R]] || wt_reds_.count(P.producer[R])) && !ew_is_absorbed(P.producer[R]);
     if (direct) {
       place(R, AR_GRAD, off);
       grad_placed.insert(R);
@@ -407,7 +407,7 @@ void Graph::plan_storage() {
     }
   bump[AR_TEMP] = temp_top;
   for (int i = 0; i < nO; ++i)
-    if (!op_done_[i]) scratch_bytes_ = std::max(scratch_bytes_, scratch_for(P, i, action_[i]));
+    if (!op_done_[i] || wt_reds_.count(i)) scratch_bytes_ = std::max(scratch_bytes_, scratch_for(P, i, action_[i]));
   bump[AR_SCRATCH] = align256(scratch_bytes_);
   if (!parent) {
     bump[AR_PARAM] = flat_floats_ * 4;

@@ -199,6 +199,18 @@ def test_softmax_gradient_row_epilogue(ctx):
     run(ctx, build, {"dp": dp, "p": p, "__prngSeed": seed})
 
 
+@pytest.mark.parametrize("n", [96, 37])
+def test_column_sum_stored_by_its_producer(ctx, n):
+    """A column sum of a tensor that an elementwise group stores for other
+    readers is computed by that group's launch (float4 columns and scalar)."""
+    x, y = rnd([300, n], 69), rnd([300, n], 70)
+
+    def build():
+        e = tg.mulScalar(tg.add(T("x", [300, n]), T("y", [300, n])), 3.0)
+        return tg.add(e, tg.sumToShape(e, [1, n]))
+    run(ctx, build, {"x": x, "y": y})
+
+
 def test_sum_to_shape_middle(ctx):
     """Reduced dims on both sides of the kept ones (the conv bias gradient
     [B, C, H, W] -> [C, 1, 1]), small and at the CNN benchmark's size."""

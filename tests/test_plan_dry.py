@@ -249,3 +249,15 @@ def test_mean_read_before_the_variance_keeps_its_own_launch():
     g = trace_fn(f)
     launches = BK.plan_dry(_program(g, {}, [], g.outputs[0], None, len(g.ops)))["launches"]
     assert "mean_last" in launches
+
+
+@pytest.mark.parametrize("n", [96, 37])
+def test_column_sum_is_stored_by_its_producer_group(n):
+    """A stored elementwise result that is also column-summed: one launch
+    writes both (the group becomes a column reduction that stores its value)."""
+    def f():
+        e = tg.mulScalar(tg.add(T("x", [300, n]), T("y", [300, n])), 3.0)
+        return tg.add(e, tg.sumToShape(e, [1, n]))
+    g = trace_fn(f)
+    launches = BK.plan_dry(_program(g, {}, [], g.outputs[0], None, len(g.ops)))["launches"]
+    assert launches[0] == "fused_red|sum_to_shape+store:add+mul_scalar" and "colsum" not in launches
