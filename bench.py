@@ -102,19 +102,17 @@ def dist_env():
     return rank, world, local
 
 
-def gemm_flops_of(program, kinds):
-    """Algorithmic FLOPs of the GEMM launches, in launch order."""
-    g = program["graph"]
-    T = g["tensors"]
+def gemm_flops_of(labels):
+    """Algorithmic FLOPs (2·M·N·K per batch entry) of the GEMM launches, read
+    from their launch labels ("matmul|M=.. N=.. K=.. b=.. ..."). Matmuls that
+    a fused kernel computes (attention) are not GEMM launches and not counted."""
     fl = []
-    for op in g["ops"]:
-        if op["kind"] in ("matmul", "matmul_batched"):
-            a, b, o = T[op["a"]]["shape"], T[op["b"]]["shape"], T[op["out"]]["shape"]
-            K = a[-1]
-            n = 1
-            for d in o:
-                n *= d
-            fl.append(2.0 * n * K)
+    for lab in labels:
+        kind, _, rest = lab.partition("|")
+        if kind not in ("matmul", "matmul_batched"):
+            continue
+        f = dict(kv.split("=", 1) for kv in rest.split() if "=" in kv)
+        fl.append(2.0 * int(f["M"]) * int(f["N"]) * int(f["K"]) * int(f.get("b", 1)))
     return fl
 
 
@@ -258,7 +256,7 @@ def main():
         by_kind[k] = by_kind.get(k, 0.0) + t
     hbm, bf16, bf16s, src = peaks()
     gemm_ms = sum(t for k, t in zip(kinds, prof) if k in ("matmul", "matmul_batched"))
-    gemm_fl = sum(gemm_flops_of(ir.program, kinds))
+    gemm_fl = sum(gemm_flops_of(labels))
     dom = max(by_kind.items(), key=lambda kv: kv[1])[0]
     n_gemm = sum(1 for k in kinds if k in ("matmul", "matmul_batched"))
     roof = {"bound": "tensor", "kernel": "matmul+matmul_batched (all GEMM launches of one step)",
