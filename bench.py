@@ -36,7 +36,7 @@ sys.path.insert(0, ROOT)
 from tensorgrad_b200 import configs as CF  # noqa: E402
 
 METRIC = "train samples/sec (GPT d384 L6 T256, config 4)"
-GEMM_DRAM_BYTES_PER_LAUNCH = 11427.5e6 / 147  # ncu capture of one step, profiles/c4_step_launches.md
+GEMM_DRAM_BYTES_PER_LAUNCH = 11404.9e6 / 147  # ncu capture of one step, profiles/c4_step_launches.md
 UNIT = "samples/s"
 
 
@@ -263,7 +263,7 @@ def main():
             "achieved": gemm_fl / (gemm_ms * 1e-3) / 1e12 if gemm_ms > 0 else None, "peak": bf16,
             "unit": "TFLOP/s", "peak_source": f"{src} bf16 dense (MEASURED_PEAKS.json)",
             # DRAM bytes per GEMM launch, averaged over the step's launches in one ncu capture
-            # (profiles/c4_step_launches.md: 11428 MB over 147 gemm_tc launches). "achieved" is
+            # (profiles/c4_step_launches.md: 11405 MB over 147 gemm_tc launches). "achieved" is
             # the same average: the step's GEMM flops over its GEMM time.
             "traffic": GEMM_DRAM_BYTES_PER_LAUNCH if args.config == "c4" and not args.batch else None,
             "traffic_unit": "bytes per launch (average over the step's GEMM launches)",
