@@ -261,3 +261,17 @@ def test_column_sum_is_stored_by_its_producer_group(n):
     g = trace_fn(f)
     launches = BK.plan_dry(_program(g, {}, [], g.outputs[0], None, len(g.ops)))["launches"]
     assert launches[0] == "fused_red|sum_to_shape+store:add+mul_scalar" and "colsum" not in launches
+
+
+@pytest.mark.parametrize("rows,merged", [(300, True), (4096, False)])
+def test_write_through_skips_large_arithmetic_heavy_groups(rows, merged):
+    """A small exp group stores its value and its column sum in one launch; a
+    large one (>= 4M elements) keeps the elementwise grid and a separate
+    column sum."""
+    def f():
+        e = tg.exp(T("x", [rows, 1024]))
+        return tg.add(e, tg.sumToShape(e, [1, 1024]))
+    g = trace_fn(f)
+    launches = BK.plan_dry(_program(g, {}, [], g.outputs[0], None, len(g.ops)))["launches"]
+    assert (launches[0] == "fused_red|sum_to_shape+store:exp") == merged
+    assert ("colsum" in launches) != merged
