@@ -234,6 +234,7 @@ class Graph {
   };
   std::vector<EwGroup> ew_groups_;
   std::map<int, int> row_values(const EwGroup& G) const;
+  bool reads_as_row(int x, const std::vector<int64_t>& vshape, int64_t len);
   std::set<int> wt_reds_;           // column reductions computed by their producer group's launch  // row value tensor -> the value it aliases
   std::vector<int> ew_group_;        // per op: group index when the op roots a group, else -1
   std::vector<char> ew_absorbed_;    // per op: value computed inside the groups that use it (no storage)

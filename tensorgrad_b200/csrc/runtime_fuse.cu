@@ -136,6 +136,22 @@ static std::set<int> view_aliases(const Program& P, int t) {
   return s;
 }
 
+// True when an elementwise group over shape vshape (rows of length len)
+// reads tensor x as one value per row: element (r, j) of the group takes
+// element r of x. A per-row value reshaped so that it broadcasts another way
+// (a [1, N] or [N] view of an [N, 1] row result over [N, N]) is not.
+bool Graph::reads_as_row(int x, const std::vector<int64_t>& vshape, int64_t len) {
+  bool dummy = true;
+  const EwInput in = ew_input(x, vshape, dummy, false);
+  if (in.mode == IN_ROWDIV) return in.period == len;
+  if (in.mode == IN_SCALAR) {
+    int64_t n = 1;
+    for (int64_t d : vshape) n *= d;
+    return n == len;  // a single row
+  }
+  return false;
+}
+
 bool Graph::ew_internal(int t) const {
   if (ew_absorbed_.empty()) return false;
   const int p = P.producer[t];
@@ -379,7 +395,11 @@ void Graph::plan_fusion() {
           bool ok = true;
           for (int m : C.members)
             for (int x : ew_operands(P, m)) {
-              if (rowvals.count(x) || cm.count(P.producer[x])) continue;
+              if (rowvals.count(x)) {
+                if (!reads_as_row(x, vshape, len)) ok = false;
+                continue;
+              }
+              if (cm.count(P.producer[x])) continue;
               const TView& vx = views_[x];
               if (vx.onehot || ew_internal(x) || P.producer[x] >= R.red) { ok = false; continue; }
               bool dummy = true;
@@ -461,11 +481,19 @@ void Graph::plan_fusion() {
         bool dummy = true;
         if (ew_input(a1, vshape, dummy, false).mode != IN_FULL) continue;
         bool ok = views_[b].root == b;
+        const std::set<int> row_readers = [&] {
+          std::set<int> s(R.members.begin(), R.members.end());
+          s.insert(R.epi.begin(), R.epi.end());
+          return s;
+        }();
         for (int y : view_aliases(P, b))
           for (int c : P.consumers[y]) {
             const bool alias = (P.kind[c] == "reshape" || P.kind[c] == "stop_gradient") &&
                                P.T[P.out[c]].numel == P.T[y].numel;
             if (alias ? !op_done_[c] : (!readers.count(c) && c <= R.red)) ok = false;
+            // the kernel hands every reader the row's value from a register,
+            // so each alias read over the row shape must index per row
+            if (!alias && row_readers.count(c) && !reads_as_row(y, vshape, len)) ok = false;
           }
         if (!ok) continue;
         R.pre = r1;

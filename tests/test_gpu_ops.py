@@ -338,3 +338,23 @@ def test_fused_reductions_and_shared_producers(ctx):
         c = tg.sub(T("x", [256, 96]), mm)
         return tg.add(tg.mul(c, c), tg.div(c, tg.sqrt(tg.addScalar(mm, 3.0))))
     run(ctx, shared, {"x": x, "m": np.abs(m)})
+
+
+@pytest.mark.parametrize("view", ["row", "flat"])
+def test_row_result_broadcast_along_columns(ctx, view):
+    """A [64, 1] row sum (and a row mean) reshaped to [1, 64] or [64]
+    broadcasts along columns: element (r, j) uses the value of row j."""
+    x, p = rnd([64, 64], 71), rnd([64, 64], 72)
+    shp = [1, 64] if view == "row" else [64]
+
+    def build_sum():
+        X, P = T("x", [64, 64]), T("p", [64, 64])
+        s = tg.reshape(tg.sum(tg.mul(X, P), -1, keepDims=True), shp)
+        return tg.mulScalar(tg.mul(tg.sub(X, s), P), 0.5)
+
+    def build_mean():
+        X = T("x", [64, 64])
+        d = tg.sub(X, tg.reshape(tg.mean(X, -1, keepDims=True), shp))
+        return tg.mean(tg.mul(d, d), -1)
+    run(ctx, build_sum, {"x": x, "p": p})
+    run(ctx, build_mean, {"x": x})

@@ -275,3 +275,41 @@ def test_write_through_skips_large_arithmetic_heavy_groups(rows, merged):
     launches = BK.plan_dry(_program(g, {}, [], g.outputs[0], None, len(g.ops)))["launches"]
     assert (launches[0] == "fused_red|sum_to_shape+store:exp") == merged
     assert ("colsum" in launches) != merged
+
+
+def _transposed_row_sum(view):
+    """mulScalar(mul(sub(X, view(sum(X*P, -1, keepDims))), P), 0.5) over a
+    square X: the row sums of shape [64, 1] seen as [1, 64] or [64], which
+    broadcast along columns, not rows."""
+    def f():
+        X, P = T("x", [64, 64]), T("p", [64, 64])
+        s = tg.sum(tg.mul(X, P), -1, keepDims=True)
+        s = tg.reshape(s, [1, 64]) if view == "row" else tg.reshape(s, [64])
+        return tg.mulScalar(tg.mul(tg.sub(X, s), P), 0.5)
+    return f
+
+
+@pytest.mark.parametrize("view", ["row", "flat"])
+def test_transposed_row_value_is_not_an_epilogue(view):
+    """A row result read through a reshape that broadcasts it along the other
+    axis cannot be handed out per row: the reader keeps its own launch."""
+    g = trace_fn(_transposed_row_sum(view))
+    launches = BK.plan_dry(_program(g, {}, [], g.outputs[0], None, len(g.ops)))["launches"]
+    assert not any("+epi:" in x for x in launches), launches
+    assert len(launches) == 2
+
+
+@pytest.mark.parametrize("view", ["row", "flat"])
+def test_transposed_mean_is_not_a_first_pass(view):
+    """A mean read through a reshape that broadcasts along columns is not
+    absorbed as the first pass of a later row reduction over the same rows."""
+    def f():
+        X = T("x", [64, 64])
+        m = tg.mean(X, -1, keepDims=True)
+        m = tg.reshape(m, [1, 64]) if view == "row" else tg.reshape(m, [64])
+        d = tg.sub(X, m)
+        return tg.mean(tg.mul(d, d), -1)
+    g = trace_fn(f)
+    launches = BK.plan_dry(_program(g, {}, [], g.outputs[0], None, len(g.ops)))["launches"]
+    assert "mean_last" in launches, launches
+    assert not any(">mean_last" in x for x in launches), launches
