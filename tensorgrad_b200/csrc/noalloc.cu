@@ -67,6 +67,12 @@ extern "C" int tg_colsum_noalloc(const float* x, float* out, int64_t outer, int6
     if (e != cudaSuccess)
       return tg::api_fail("CudaError", std::string("tg_colsum_noalloc: scratch lookup: ") + cudaGetErrorString(e));
   }
+  // An error left pending by earlier, unrelated work on this thread is
+  // reported as such, so the check after the launch covers only this call.
+  cudaError_t pending = cudaGetLastError();
+  if (pending != cudaSuccess)
+    return tg::api_fail("CudaError", std::string("tg_colsum_noalloc: error pending from earlier work, not launched: ") +
+                                         cudaGetErrorString(pending));
   // Every partial sum is written before it is read, so nothing in the array
   // needs clearing between calls.
   tg::launch_colsum(x, out, outer, inner, scratch, reinterpret_cast<cudaStream_t>(stream));

@@ -45,12 +45,13 @@ def test_colsum_noalloc_matches_regular_path(ctx):
 
 
 def test_colsum_noalloc_extreme_shapes(ctx):
-    """The chunking bounds the partial sums (chunks x columns) by about four
-    blocks per SM, so very wide rows and very long columns both fit the fixed
-    scratch array and match the regular path."""
+    """The chunking bounds the partial sums: chunks x columns <= 4 x SMs x 128
+    + columns, which stays under the fixed array for up to 256 SMs. Very wide
+    rows, very long columns and the worst case on 148 SMs ([128, 75648]: two
+    chunks of 75648 columns, 151296 partial sums) match the regular path."""
     import torch
     lib = BK.load()
-    for outer, inner, seed in [(64, 140000, 52), (200000, 3, 53)]:
+    for outer, inner, seed in [(64, 140000, 52), (200000, 3, 53), (128, 75648, 54)]:
         x = rnd([outer, inner], seed)
         ref = run(ctx, lambda: tg.sumToShape(T("x", [outer, inner]), [inner]), {"x": x})
         np.testing.assert_array_equal(_noalloc(lib, torch, x), ref)
