@@ -88,6 +88,22 @@ class OracleTrainer:
         merged.update(injected)
         return eval_graph(self.g, merged, self.dp_rank)
 
+    def f32_grads(self, inputs: Dict[str, np.ndarray], params: Dict[str, np.ndarray],
+                  states: Dict[str, np.ndarray]) -> Dict[str, np.ndarray]:
+        """The gradients of the step just taken from ``params`` and
+        ``states``, re-evaluated with f32 arithmetic throughout (same injected
+        scalars; nothing is updated): the f32 error floor of the graph."""
+        t, prng = self.t, self.prng
+        self.t, self.prng = t - 1, (prng - 1 if self.p.get("usesPrng") else prng)
+        injected = self.scalars()
+        self.t, self.prng = t, prng
+        merged = dict(params)
+        merged.update(states)
+        merged.update(inputs)
+        merged.update(injected)
+        vals = eval_graph(self.g, merged, self.dp_rank, np.float32)
+        return {n: vals[tid] for n, tid in self.p["paramGrads"].items()}
+
     def apply_writebacks(self, vals: Dict[int, np.ndarray]) -> None:
         for wb in self.p["writebacks"]:
             dst = self.params if wb["destKind"] == "param" else self.states

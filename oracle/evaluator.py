@@ -33,6 +33,10 @@ import numpy as np
 
 F32 = np.float32
 F64 = np.float64
+# Accumulation type of vf() operands. f64 is the oracle; the tests switch it
+# to f32 (eval_graph(..., accum=np.float32)) only to measure how far any f32
+# evaluation of the same graph lands from the f64 one.
+_ACC = [F64]
 
 
 def _np_dtype(dt: str):
@@ -135,7 +139,7 @@ def eval_op(op: dict, vals: Dict[int, np.ndarray], inputs: Dict[str, np.ndarray]
         return vals[i]
 
     def vf(i):
-        return vals[i].astype(F64)
+        return vals[i].astype(_ACC[0])
 
     if k in ("param_input", "tensor_input"):
         if op["name"] not in inputs:
@@ -334,9 +338,16 @@ def eval_op(op: dict, vals: Dict[int, np.ndarray], inputs: Dict[str, np.ndarray]
     raise ValueError(f"eval: unhandled op kind {k}")
 
 
-def eval_graph(g: dict, inputs: Dict[str, np.ndarray], dp_rank: int = 0) -> Dict[int, np.ndarray]:
-    """Evaluate every op in order (test/_eval.ts:21-27)."""
+def eval_graph(g: dict, inputs: Dict[str, np.ndarray], dp_rank: int = 0, accum=F64) -> Dict[int, np.ndarray]:
+    """Evaluate every op in order (test/_eval.ts:21-27). ``accum`` is the
+    arithmetic type of elementwise ops, reductions and contractions: f64 for
+    the oracle; f32 gives a plain single-precision CPU evaluation whose
+    distance from the oracle is the f32 error floor of the graph."""
     vals: Dict[int, np.ndarray] = {}
-    for op in g["ops"]:
-        vals[op["out"]] = eval_op(op, vals, inputs, g, dp_rank)
+    prev, _ACC[0] = _ACC[0], accum
+    try:
+        for op in g["ops"]:
+            vals[op["out"]] = eval_op(op, vals, inputs, g, dp_rank)
+    finally:
+        _ACC[0] = prev
     return vals

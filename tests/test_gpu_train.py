@@ -28,7 +28,7 @@ from tensorgrad_b200 import backend as BK
 from tensorgrad_b200 import configs as CF
 from tensorgrad_b200.compile import build_training_ir, initial_params
 
-from .test_gpu_ops import close
+from .test_gpu_ops import RTOL, close
 
 pytestmark = pytest.mark.gpu
 
@@ -122,7 +122,22 @@ def test_fused_attention_train_parity(ctx, over, monkeypatch):
     _parity(ctx, "c4", 2, **over)
 
 
-def _parity(ctx, name, steps, **over):
+def floor_needed(gpu, ref, rtol=RTOL):
+    """Smallest f with |gpu - ref| <= rtol * max(|ref|, f * max|ref|) for
+    every element: 0 means every element meets rtol relative to itself."""
+    gpu = np.asarray(gpu, np.float64).reshape(-1)
+    ref = np.asarray(ref, np.float64).reshape(-1)
+    m = max(np.abs(ref).max(), 1e-30)
+    need = np.max(np.abs(gpu - ref) / rtol - np.abs(ref))
+    return float(max(need, 0.0) / m)
+
+
+def _parity(ctx, name, steps, record=None, grad_frac=1.0, f32_floor=False, **over):
+    """Step-by-step parity. record(kind, tensor, step, floor) receives the
+    per-element floor each compared tensor needed (see floor_needed); with
+    f32_floor, also ("grad_f32cpu", ...) for a plain f32 CPU evaluation of
+    the same step, the floor any f32 implementation of the graph reaches."""
+    rec = record or (lambda *a: None)
     w, ir, dg, orc, data = setup(ctx, name, **over)
     if name in ("c4", "c5"):
         kinds = [x.split("|")[0] for x in dg.launch_list()]
@@ -139,13 +154,18 @@ def _parity(ctx, name, steps, **over):
             orc.t, orc.prng = t - 1, t - 1
             lg, _ = dg.step(data)
             lo = orc.step(data)
+            rec("loss", "loss", t, floor_needed([lg], [lo]))
             close([lg], [lo])
             og = orc.grads()
+            if f32_floor:
+                for n, g32 in orc.f32_grads(data, p_before, s_before).items():
+                    rec("grad_f32cpu", n, t, floor_needed(g32, og[n]))
             gg = {}
             for n, shp in shapes.items():
                 gg[n] = dg.read_grad(n, shp)
+                rec("grad", n, t, floor_needed(gg[n], og[n]))
                 try:
-                    close(gg[n], og[n].reshape(shp), tensor_frac=1.0)
+                    close(gg[n], og[n].reshape(shp), tensor_frac=grad_frac)
                 except AssertionError as e:
                     raise AssertionError(f"step {t} grad {n}: {e}")
             p_after = dg.download_params(shapes)
@@ -153,11 +173,13 @@ def _parity(ctx, name, steps, **over):
             ref_p, ref_s = reference_update(ir.program, t, {k: v.astype(np.float64) for k, v in p_before.items()},
                                             {k: v.astype(np.float64) for k, v in s_before.items()}, gg)
             for n in shapes:
+                rec("param", n, t, floor_needed(p_after[n], ref_p[n]))
                 try:
                     close(p_after[n], ref_p[n])
                 except AssertionError as e:
                     raise AssertionError(f"step {t} param {n}: {e}")
             for n in ref_s:
+                rec("state", n, t, floor_needed(s_after[n], ref_s[n]))
                 close(s_after[n], ref_s[n].reshape(s_after[n].shape))
     finally:
         dg.destroy()
