@@ -36,8 +36,11 @@ sys.path.insert(0, ROOT)
 from tensorgrad_b200 import configs as CF  # noqa: E402
 
 METRIC = "train samples/sec (GPT d384 L6 T256, config 4)"
-GEMM_DRAM_BYTES_PER_LAUNCH = 11404.9e6 / 147  # ncu capture of one step, profiles/c4_step_launches.md
 UNIT = "samples/s"
+# launch classes whose roofline is HBM bandwidth (their algorithmic bytes come
+# from the planner, tg_launch_bytes)
+MEMORY_BOUND = ("fused_ew", "fused_red", "softmax_causal_last+dropout", "softmax_causal_last", "log_softmax_last",
+                "colsum", "rowsum", "dropout", "adam_flat", "sgd_flat", "gather_rows", "embedding_grad")
 
 
 def peaks():
@@ -116,6 +119,49 @@ def gemm_flops_of(labels):
     return fl
 
 
+def ncu_traffic(csv_path, kernel_regex):
+    """Mean dram__bytes_read.sum + dram__bytes_write.sum per launch of the
+    kernels matching kernel_regex in an `ncu --csv --page raw` export."""
+    import csv
+    import re
+    rows = list(csv.reader(open(csv_path)))
+    hdr = next(i for i, r in enumerate(rows) if "Kernel Name" in r)
+    h = rows[hdr]
+    kn, rd, wr = h.index("Kernel Name"), h.index("dram__bytes_read.sum"), h.index("dram__bytes_write.sum")
+    unit = rows[hdr + 1] if rows[hdr + 1] and rows[hdr + 1][kn] == "" else None
+    scale = {"byte": 1, "Kbyte": 1e3, "Mbyte": 1e6, "Gbyte": 1e9}
+    tot = []
+    for r in rows[hdr + 1 + (1 if unit else 0):]:
+        if len(r) > max(kn, rd, wr) and re.search(kernel_regex, r[kn]):
+            f = lambda c: float(r[c].replace(",", "")) * (scale.get(unit[c], 1) if unit else 1)
+            tot.append(f(rd) + f(wr))
+    return sum(tot) / len(tot) if tot else None
+
+
+def memory_bound_rooflines(labels, prof, nbytes, hbm):
+    """Per class of HBM-bound launches: algorithmic bytes of one step, the
+    class's live event time, achieved GB/s and its fraction of the measured
+    copy bandwidth."""
+    out, tb, tm = {}, 0.0, 0.0
+    for lab, t, b in zip(labels, prof, nbytes):
+        k = lab.split("|")[0]
+        if k not in MEMORY_BOUND or b <= 0:
+            continue
+        c = out.setdefault(k, {"launches": 0, "bytes": 0.0, "ms": 0.0})
+        c["launches"] += 1
+        c["bytes"] += b
+        c["ms"] += t
+        tb += b
+        tm += t
+    for c in out.values():
+        c["gbs"] = c["bytes"] / (c["ms"] * 1e-3) / 1e9 if c["ms"] > 0 else None
+        c["frac"] = c["gbs"] / hbm if c["gbs"] else None
+    out = dict(sorted(out.items(), key=lambda kv: -kv[1]["ms"]))
+    out["all"] = {"bytes": tb, "ms": tm, "gbs": tb / (tm * 1e-3) / 1e9 if tm > 0 else None,
+                  "frac": tb / (tm * 1e-3) / 1e9 / hbm if tm > 0 else None}
+    return out
+
+
 def cpu_baseline(w, sample_batch: int, threads: int):
     """Times one oracle training step on `sample_batch` sequences."""
     from oracle.driver import OracleTrainer
@@ -176,6 +222,9 @@ def main():
                     help="sequences per GPU (default: the config's; smaller only for profiling captures)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--profile-out", default=None, help="write per-launch (label, ms) of one profiled step as JSON")
+    ap.add_argument("--traffic-csv", default=None,
+                    help="ncu --csv --page raw export of GEMM launches of this workload (dram__bytes_read/write): "
+                         "fills roofline.traffic; without it traffic is null")
     args = ap.parse_args()
     w = CF.workload(args.config, **({"batch": args.batch} if args.batch else {}))
     if args.impl == "reference":
@@ -262,16 +311,16 @@ def main():
     roof = {"bound": "tensor", "kernel": "matmul+matmul_batched (all GEMM launches of one step)",
             "achieved": gemm_fl / (gemm_ms * 1e-3) / 1e12 if gemm_ms > 0 else None, "peak": bf16,
             "unit": "TFLOP/s", "peak_source": f"{src} bf16 dense (MEASURED_PEAKS.json)",
-            # DRAM bytes per GEMM launch, averaged over the step's launches in one ncu capture
-            # (profiles/c4_step_launches.md: 11405 MB over 147 gemm_tc launches). "achieved" is
-            # the same average: the step's GEMM flops over its GEMM time.
-            "traffic": GEMM_DRAM_BYTES_PER_LAUNCH if args.config == "c4" and not args.batch else None,
-            "traffic_unit": "bytes per launch (average over the step's GEMM launches)",
+            # DRAM bytes per GEMM launch from an ncu capture of this workload, when one is given
+            "traffic": ncu_traffic(args.traffic_csv, r"gemm_tc") if args.traffic_csv else None,
+            "traffic_unit": "bytes per launch (average over the captured GEMM launches)",
             "gemm_launches_per_step": n_gemm}
     roof["frac"] = roof["achieved"] / bf16 if roof["achieved"] else None
     roof["frac_of_3xtf32_effective"] = roof["achieved"] / (bf16 / 6.0) if roof["achieved"] else None
     roof["dominant_kind"] = dom
     roof["step_share"] = {k: round(v / sum(prof), 4) for k, v in sorted(by_kind.items(), key=lambda kv: -kv[1])[:8]}
+    roof["memory_bound"] = memory_bound_rooflines(labels, prof, dg.launch_bytes(), hbm)
+    roof["memory_bound_peak_gbs"] = hbm
 
     value = args.steps * gb / (ms * 1e-3)
     e2e = args.steps * gb / (e2e_ms * 1e-3)

@@ -121,6 +121,13 @@ int tg_plan_dry(const char* program_json, size_t len, int world, char* buf, size
  * writes per-launch milliseconds (in tg_launch_list order). */
 int tg_profile_step(tg_ctx* ctx, int graph_id, float* ms_out, int cap, int* n_out);
 
+/* Algorithmic bytes of every launch of one step, in tg_launch_list order:
+ * each distinct tensor the launch reads counted once at its own size, plus
+ * every tensor it writes; 0 for launches not accounted in bytes (GEMMs,
+ * convolutions, collectives). Divided by tg_profile_step's times it gives
+ * each memory-bound kernel's achieved bandwidth. (new: measurement) */
+int tg_launch_bytes(tg_ctx* ctx, int graph_id, double* out, int cap, int* n_out);
+
 /* Error code recorded by a tcgen05 GEMM whose bounded barrier wait ran out
  * (0 = none); reset != 0 clears it. (new: kernel health check for tests) */
 int tg_debug_gemm_error(int reset);

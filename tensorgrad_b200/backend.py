@@ -22,7 +22,7 @@ EXPORTED = [
     "tg_upload_params", "tg_download_params", "tg_upload_states", "tg_download_states", "tg_get_counters",
     "tg_set_counters", "tg_step", "tg_run", "tg_set_inputs", "tg_launch_step",
     "tg_read_loss", "tg_stream", "tg_reset_optimizer", "tg_set_lr", "tg_destroy_graph", "tg_read_grad",
-    "tg_read_tensor", "tg_launch_list", "tg_profile_step", "tg_debug_gemm_error", "tg_debug_gemm_dbg", "tg_debug_gemm_trace", "tg_colsum_noalloc", "tg_plan_dry", "tg_last_error_name", "tg_last_error_message",
+    "tg_read_tensor", "tg_launch_list", "tg_profile_step", "tg_launch_bytes", "tg_debug_gemm_error", "tg_debug_gemm_dbg", "tg_debug_gemm_trace", "tg_colsum_noalloc", "tg_plan_dry", "tg_last_error_name", "tg_last_error_message",
 ]
 
 
@@ -80,6 +80,7 @@ def load(path: str = LIB_PATH):
         "tg_read_grad": [vp, ip, C.c_char_p, vp],
         "tg_read_tensor": [vp, ip, ip, vp],
         "tg_profile_step": [vp, ip, C.POINTER(C.c_float), ip, C.POINTER(C.c_int)],
+        "tg_launch_bytes": [vp, ip, C.POINTER(C.c_double), ip, C.POINTER(C.c_int)],
         "tg_debug_gemm_error": [ip],
         "tg_debug_gemm_dbg": [C.POINTER(C.c_int)],
         "tg_debug_gemm_trace": [C.POINTER(C.c_longlong), ip],
@@ -193,6 +194,15 @@ class DeviceGraph:
         cap = 1 << 16
         buf = (C.c_float * cap)()
         _check(self.lib.tg_profile_step(self.ctx.h, self.id, buf, cap, C.byref(n)))
+        return [buf[i] for i in range(min(n.value, cap))]
+
+    def launch_bytes(self) -> List[float]:
+        """Algorithmic bytes per launch (0 where not accounted), in
+        launch_list order."""
+        n = C.c_int()
+        cap = 1 << 16
+        buf = (C.c_double * cap)()
+        _check(self.lib.tg_launch_bytes(self.ctx.h, self.id, buf, cap, C.byref(n)))
         return [buf[i] for i in range(min(n.value, cap))]
 
     # -- params -----------------------------------------------------------

@@ -138,6 +138,8 @@ int tg_plan_dry(const char* program_json, size_t len, int world, char* buf, size
       first = false;
       s += q(kinds.substr(st, e - st));
     }
+    s += "],\"launchBytes\":[";
+    for (size_t i = 0; i < g.launch_bytes().size(); ++i) s += (i ? "," : "") + std::to_string(g.launch_bytes()[i]);
     s += "],\"kernelSources\":[";
     for (size_t i = 0; i < g.jit_sources().size(); ++i) s += (i ? "," : "") + q(g.jit_sources()[i]);
     s += "],\"kernelPreamble\":" + q(tg::jit_preamble()) + "}";
@@ -262,6 +264,14 @@ int tg_profile_step(tg_ctx* ctx, int graph_id, float* ms_out, int cap, int* n_ou
     get_graph(ctx, graph_id)->profile_step(ms);
     if (n_out) *n_out = (int)ms.size();
     for (int i = 0; i < cap && i < (int)ms.size(); ++i) ms_out[i] = ms[i];
+  });
+}
+
+int tg_launch_bytes(tg_ctx* ctx, int graph_id, double* out, int cap, int* n_out) {
+  return guarded([&] {
+    const auto& b = get_graph(ctx, graph_id)->launch_bytes();
+    if (n_out) *n_out = (int)b.size();
+    for (int i = 0; i < cap && i < (int)b.size(); ++i) out[i] = b[i];
   });
 }
 

@@ -119,6 +119,11 @@ struct StorageLoc {
 
 class Context;
 
+// Elementwise op kinds, and an elementwise op's operand tensors in the order
+// its expression reads them (runtime_fuse.cu).
+const std::set<std::string>& ew_kinds();
+std::vector<int> ew_operands(const Program& P, int i);
+
 class Graph {
  public:
   Graph(Context* ctx, int id, Graph* parent, const char* json, size_t len);
@@ -153,6 +158,10 @@ class Graph {
   int64_t param_numel(const std::string& name) const;
   int launches_per_step() const { return (int)launches_.size(); }
   std::string launch_kinds() const;
+  // Algorithmic bytes of each launch (each distinct tensor read once plus
+  // every tensor written once), 0 where not accounted (GEMMs, collectives,
+  // convolutions): the numerator of the memory-bound rooflines.
+  const std::vector<double>& launch_bytes() const { return launch_bytes_; }
   const std::vector<std::string>& jit_sources() const { return jit_sources_; }
   // Runs one step launch by launch (no CUDA graph) with events around each
   // launch; fills per-launch milliseconds.
@@ -260,7 +269,9 @@ class Graph {
   int64_t prng_ = 0;
   std::vector<std::function<void(cudaStream_t)>> launches_;
   std::vector<std::string> launch_kind_;
-  std::vector<std::function<void(cudaStream_t)>> post_;  // writebacks
+  std::vector<double> launch_bytes_;
+  double next_bytes_ = 0;  // bytes of the next add()ed launch
+  double tensor_bytes(int t) const;  std::vector<std::function<void(cudaStream_t)>> post_;  // writebacks
   cudaGraph_t cgraph_ = nullptr;
   cudaGraphExec_t cexec_ = nullptr;
   bool use_graph_ = true;

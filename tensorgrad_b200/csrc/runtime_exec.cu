@@ -559,9 +559,17 @@ EwInput Graph::ew_input(int t, const std::vector<int64_t>& oshape, bool& vec_ok,
   return in;
 }
 
+double Graph::tensor_bytes(int t) const {
+  const TView& v = views_[t];
+  if (v.onehot) return 4.0 * (double)P.T[v.onehot_idx].numel;  // a virtual one-hot reads its indices
+  return 4.0 * (double)P.T[t].numel;
+}
+
 void Graph::emit_launches() {
   launches_.clear();
   launch_kind_.clear();
+  launch_bytes_.clear();
+  next_bytes_ = 0;
   post_.clear();
   const int nO = (int)P.ops.size();
   float* scratch = reinterpret_cast<float*>(arena_[AR_SCRATCH]);
@@ -573,6 +581,8 @@ void Graph::emit_launches() {
   auto add = [&](const std::string& kind, std::function<void(cudaStream_t)> f) {
     launches_.push_back(std::move(f));
     launch_kind_.push_back(kind);
+    launch_bytes_.push_back(next_bytes_);
+    next_bytes_ = 0;
   };
 
   auto mk_input = [&](int t, const std::vector<int64_t>& oshape, bool& vec_ok) -> EwInput {
@@ -640,6 +650,18 @@ void Graph::emit_launches() {
     const auto& O = P.op(i);
     int o = P.out[i];
     const auto& os = P.T[o].shape;
+    next_bytes_ = 0;
+    if (ew_kinds().count(k) || k == "reshape" || k == "stop_gradient" || k == "sum_to_shape" || k == "permute" ||
+        k == "mean_last" || k == "sum_last" || k == "max_last" || k == "argmax_last" || k == "log_softmax_last" ||
+        k == "softmax_causal_last" || k == "categorical_last") {
+      std::set<int> rd;
+      if (ew_kinds().count(k)) for (int t : ew_operands(P, i)) rd.insert(t);
+      else rd.insert(O["a"].i32());
+      for (int t : rd) next_bytes_ += tensor_bytes(t);
+      next_bytes_ += tensor_bytes(o);
+      auto sd = softmax_drop_.find(i);
+      if (sd != softmax_drop_.end()) next_bytes_ += tensor_bytes(P.out[sd->second]);
+    }
     if (action_[i] == 110 || action_[i] == 111) {
       const AttnBlock& A = attn_[attn_of_.at(i)];
       auto aview = [&](int t, bool swap_last) {
@@ -683,6 +705,7 @@ void Graph::emit_launches() {
       const float* gp = reinterpret_cast<const float*>(ptr(g));
       const int* ip = reinterpret_cast<const int*>(ptr(idx));
       float* op = reinterpret_cast<float*>(ptr(o));
+      next_bytes_ = 4.0 * (double)(P.T[g].numel + P.T[idx].numel + P.T[o].numel);
       add("row_hit", [=](cudaStream_t s) { launch_row_hit(gp, ip, op, rows, V, s); });
       continue;
     }
@@ -695,6 +718,7 @@ void Graph::emit_launches() {
       const float* xp = reinterpret_cast<const float*>(ptr(x));
       const int* ip = reinterpret_cast<const int*>(ptr(idx));
       float* op = reinterpret_cast<float*>(ptr(o));
+      next_bytes_ = 4.0 * (double)(rows + P.T[idx].numel + P.T[o].numel);  // one element read per row
       add("pick", [=](cudaStream_t s) { launch_pick(xp, ip, op, rows, V, s); });
       continue;
     }
@@ -706,6 +730,7 @@ void Graph::emit_launches() {
       const int* ip = reinterpret_cast<const int*>(ptr(idx));
       const float* tp = reinterpret_cast<const float*>(ptr(b));
       float* op = reinterpret_cast<float*>(ptr(o));
+      next_bytes_ = 4.0 * (double)(rows + 2 * rows * D);  // indices, gathered rows, output
       add("gather_rows", [=](cudaStream_t s) { launch_gather_rows(ip, tp, op, rows, V, D, s); });
       continue;
     }
@@ -719,6 +744,7 @@ void Graph::emit_launches() {
       const float* dyp = reinterpret_cast<const float*>(ptr(b));
       float* op = reinterpret_cast<float*>(ptr(o));
       int* scr = reinterpret_cast<int*>(scratch);
+      next_bytes_ = 4.0 * (double)(rows + rows * D + V * D);  // indices, row gradients, table gradient
       add("embedding_grad", [=](cudaStream_t s) { launch_embedding_grad(ip, dyp, op, rows, V, D, scr, s); });
       continue;
     }
@@ -1124,6 +1150,7 @@ void Graph::emit_launches() {
     d.lrt = reinterpret_cast<const float*>(ptr(adam_lrt_));
     d.shrink_dev = adam_shrink_ >= 0 ? reinterpret_cast<const float*>(ptr(adam_shrink_)) : nullptr;
     d.grad_scale = gscale;
+    next_bytes_ = 28.0 * (double)flat_floats_;  // read p, g, m, v; write p, m, v
     add("adam_flat", [d](cudaStream_t s) { launch_adam_flat(d, s); });
   } else if (sgd_fused_) {
     SgdFlatDesc d = sgd_;
@@ -1134,6 +1161,7 @@ void Graph::emit_launches() {
     d.n_decay = n_decay_;
     d.lr = reinterpret_cast<const float*>(ptr(sgd_lr_));
     d.grad_scale = gscale;
+    next_bytes_ = (sgd_.momentum > 0 ? 20.0 : 12.0) * (double)flat_floats_;
     add("sgd_flat", [d](cudaStream_t s) { launch_sgd_flat(d, s); });
   } else {
     // Unfused optimizer graph: copy each new value to its home after all ops.

@@ -38,6 +38,8 @@ bool jit_enabled() {
   return !(e && e[0] == '0');
 }
 
+}  // namespace
+
 const std::set<std::string>& ew_kinds() {
   static const std::set<std::string> s = {
       "add", "sub", "mul", "div", "min", "max", "less", "greater",
@@ -65,6 +67,8 @@ std::vector<int> ew_operands(const Program& P, int i) {
   if (binary.count(k)) return {O["a"].i32(), O["b"].i32()};
   return {O["a"].i32()};
 }
+
+namespace {
 
 // Exact f32 literal in generated source.
 std::string lit(float f) {
@@ -623,6 +627,7 @@ void Graph::emit_ew_group(int gi, const int* seed_ptr, float* scratch, size_t sc
   // length is a multiple of 4 (four adjacent columns per thread)
   bool vec = rs == RED_NONE || (rs == RED_COL && len % 4 == 0);
   std::vector<EwInput> ins;
+  std::set<int> reads;  // distinct tensors the launch reads, for its byte count
   std::map<int, int> slot_of;
   bool has_drop = false;
   std::ostringstream ops;
@@ -633,6 +638,7 @@ void Graph::emit_ew_group(int gi, const int* seed_ptr, float* scratch, size_t sc
   if (G.pre >= 0) {
     pre_slot = (int)ins.size();
     ins.push_back(ew_input(P.op(G.pre)["a"].i32(), os, vec));
+    reads.insert(P.op(G.pre)["a"].i32());
   }
   for (int m : G.members) {
     std::vector<std::string> a;
@@ -642,6 +648,7 @@ void Graph::emit_ew_group(int gi, const int* seed_ptr, float* scratch, size_t sc
       if (it == slot_of.end()) {
         it = slot_of.emplace(t, (int)ins.size()).first;
         ins.push_back(ew_input(t, os, vec));
+        reads.insert(t);
       }
       a.push_back("x" + std::to_string(it->second));
     }
@@ -723,6 +730,7 @@ void Graph::emit_ew_group(int gi, const int* seed_ptr, float* scratch, size_t sc
           in.ptr = ptr(x);
           in.mode = P.T[x].numel == 1 ? IN_SCALAR : IN_FULL;
           ins.push_back(in);
+          reads.insert(x);
           post << "      const float y" << it->second << " = __ldg(p" << it->second
                << (P.T[x].numel == 1 ? ")" : " + r)") << ";\n";
         }
@@ -754,6 +762,7 @@ void Graph::emit_ew_group(int gi, const int* seed_ptr, float* scratch, size_t sc
           EwInput in = ew_input(x, os, dummy);
           it = eslot.emplace(x, (int)ins.size()).first;
           ins.push_back(in);
+          reads.insert(x);
           const std::string pp = "p" + std::to_string(it->second), per = std::to_string(in.period) + "ll";
           std::string ld;
           if (in.mode == IN_FULL) ld = "__ldg(" + pp + " + e)";
@@ -931,6 +940,17 @@ void Graph::emit_ew_group(int gi, const int* seed_ptr, float* scratch, size_t sc
     label = "fused_red|" + (G.pre >= 0 ? P.kind[G.pre] + ">" : std::string()) + P.kind[G.red] +
             (G.wt >= 0 ? "+store" : "") + ":" + label.substr(0, 150);
   else if (G.members.size() > 1) label = "fused_ew|" + label.substr(0, 160);
+  // algorithmic bytes: each distinct input once, every output once
+  {
+    double b = 0;
+    for (int t : reads) b += tensor_bytes(t);
+    b += tensor_bytes(P.out[G.root]);
+    if (has_post) for (int pr : G.post_roots) b += tensor_bytes(P.out[pr]);
+    if (has_epi) b += tensor_bytes(P.out[G.epi_root]);
+    if (G.pre >= 0) b += tensor_bytes(P.out[G.pre]);
+    if (G.wt >= 0) b += tensor_bytes(P.out[G.wt]);
+    next_bytes_ = b;
+  }
   float* fold_out = reinterpret_cast<float*>(out);
   const int64_t fold_n = (rs == RED_COL && nchunk > 1) ? nchunk : 0, fold_len = len;
   float* fold_part = scratch;

@@ -56,6 +56,29 @@ def test_checkpoint_resume_continues_the_run(ctx):
     b.destroy()
 
 
+def test_checkpoint_resumes_the_oracle_run(ctx):
+    """A checkpoint loaded into the CPU oracle (params, moments, the step and
+    dropout counters from its metadata) continues the run as the GPU does:
+    the next two losses and the params after them agree at the op
+    tolerance."""
+    from oracle.driver import OracleTrainer
+    w, a = _train(ctx, seed=1)
+    for i in range(3):
+        _step(a, _batch(w, i))
+    d = tg.loadSafetensors(a.exportCheckpoint())
+    meta = d["metadata"]
+    orc = OracleTrainer(a.program, {n[6:]: v for n, v in d["tensors"].items() if n.startswith("param/")})
+    orc.states = {n[6:]: v.reshape(orc.states[n[6:]].shape) for n, v in d["tensors"].items()
+                  if n.startswith("state/")}
+    orc.t, orc.prng = int(meta["step"]), int(meta["prng"])
+    for i in (3, 4):
+        close([_step(a, _batch(w, i))], [orc.step(_batch(w, i))])
+    got = a.downloadParams()
+    for n, v in orc.params.items():
+        close(got[n], v.reshape(got[n].shape))
+    a.destroy()
+
+
 def test_checkpoint_import_is_strict(ctx):
     w, a = _train(ctx, seed=1)
     blob = a.exportCheckpoint()

@@ -313,3 +313,19 @@ def test_transposed_mean_is_not_a_first_pass(view):
     launches = BK.plan_dry(_program(g, {}, [], g.outputs[0], None, len(g.ops)))["launches"]
     assert "mean_last" in launches, launches
     assert not any(">mean_last" in x for x in launches), launches
+
+
+def test_launch_bytes_count_each_tensor_once():
+    """The planner's algorithmic bytes per launch: distinct inputs at their own
+    size (a broadcast row once) plus every output."""
+    def f():
+        x, b = T("x", [64, 48]), T("b", [48])
+        return tg.tanh(tg.add(tg.mul(x, x), b))
+    g = trace_fn(f)
+    r = BK.plan_dry(_program(g, {}, [], g.outputs[0], None, len(g.ops)))
+    assert r["launches"] == ["fused_ew|mul+add+tanh"]
+    assert r["launchBytes"] == [4.0 * (64 * 48 + 48 + 64 * 48)]
+    c4 = plan("c4")
+    by = dict(zip(kinds(c4), c4["launchBytes"]))
+    assert by["adam_flat"] > 0 and by["colsum"] > 0 and by["gather_rows"] > 0
+    assert all(b == 0 for k, b in zip(kinds(c4), c4["launchBytes"]) if k.startswith("matmul"))
