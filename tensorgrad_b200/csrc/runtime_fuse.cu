@@ -639,6 +639,7 @@ void Graph::emit_ew_group(int gi, const int* seed_ptr, float* scratch, size_t sc
     pre_slot = (int)ins.size();
     ins.push_back(ew_input(P.op(G.pre)["a"].i32(), os, vec));
     reads.insert(P.op(G.pre)["a"].i32());
+    slot_of.emplace(P.op(G.pre)["a"].i32(), pre_slot);
   }
   for (int m : G.members) {
     std::vector<std::string> a;
@@ -667,6 +668,33 @@ void Graph::emit_ew_group(int gi, const int* seed_ptr, float* scratch, size_t sc
   const int64_t col_chunks = rs == RED_COL ? colsum_chunks(rows, len) : 1;
   const int R = (int)os.size();
 
+  // Register-cached rows (warp-per-row reductions over rows of 32·KJ
+  // elements): each lane loads its KJ elements of every full-size input once
+  // per row into registers, all loads of a row in flight together, and every
+  // pass over the row (first-pass mean, the reduction, the epilogue) reads
+  // them from there; inputs that repeat along rows (LayerNorm's gain and
+  // bias) are loaded once per warp, per-row scalars once per row. The
+  // arithmetic and its order are the uncached kernel's, so results are
+  // bit-identical.
+  const bool rowc = rs == RED_ROW && len <= kWarpRowMax && len % 32 == 0;
+  const int64_t KJ = rowc ? len / 32 : 0;
+  int64_t cache_budget = rowc ? 72 : 0;  // cached floats per lane
+  std::vector<int> cmode;                // per slot: 0 load, 1 row array, 2 column array, 3 row scalar
+  auto cache_slot = [&](int si) {
+    if ((int)cmode.size() <= si) cmode.resize(si + 1, 0);
+    if (!rowc) return;
+    const EwInput& in = ins[si];
+    if (in.mode == IN_ROWDIV && in.period == len) cmode[si] = 3;
+    else if ((in.mode == IN_FULL || (in.mode == IN_PERIOD && in.period == len)) && cache_budget >= KJ) {
+      cmode[si] = in.mode == IN_FULL ? 1 : 2;
+      cache_budget -= KJ;
+    }
+  };
+  auto cached_ref = [&](int si) -> std::string {
+    return cmode[si] == 3 ? "s" + std::to_string(si) : "c" + std::to_string(si) + "[jj]";
+  };
+  if (pre_slot >= 0) cache_slot(pre_slot);
+
   // Per-element values of each input: for the vector form, loads before the
   // 4-lane loop plus per-lane picks; otherwise one load per element index e.
   std::ostringstream pre, lane;
@@ -674,6 +702,11 @@ void Graph::emit_ew_group(int gi, const int* seed_ptr, float* scratch, size_t sc
     const EwInput& in = ins[si];
     std::string p = "p" + std::to_string(si), x = "x" + std::to_string(si);
     std::string per = std::to_string(in.period) + "ll";
+    if ((int)si != pre_slot) cache_slot((int)si);
+    if (cmode[si]) {
+      lane << "      const float " << x << " = " << cached_ref((int)si) << ";\n";
+      continue;
+    }
     switch (in.mode) {
       case IN_FULL:
         if (vec) { pre << "    const float4 q" << si << " = __ldg(reinterpret_cast<const float4*>(" << p << " + i));\n";
@@ -731,6 +764,7 @@ void Graph::emit_ew_group(int gi, const int* seed_ptr, float* scratch, size_t sc
           in.mode = P.T[x].numel == 1 ? IN_SCALAR : IN_FULL;
           ins.push_back(in);
           reads.insert(x);
+          cmode.resize(ins.size(), 0);
           post << "      const float y" << it->second << " = __ldg(p" << it->second
                << (P.T[x].numel == 1 ? ")" : " + r)") << ";\n";
         }
@@ -760,12 +794,20 @@ void Graph::emit_ew_group(int gi, const int* seed_ptr, float* scratch, size_t sc
         if (it == eslot.end()) {
           bool dummy = true;
           EwInput in = ew_input(x, os, dummy);
-          it = eslot.emplace(x, (int)ins.size()).first;
-          ins.push_back(in);
-          reads.insert(x);
-          const std::string pp = "p" + std::to_string(it->second), per = std::to_string(in.period) + "ll";
+          auto shared = slot_of.find(x);  // an input the row pass reads already
+          if (shared != slot_of.end()) {
+            it = eslot.emplace(x, shared->second).first;
+          } else {
+            it = eslot.emplace(x, (int)ins.size()).first;
+            ins.push_back(in);
+            reads.insert(x);
+            cache_slot(it->second);
+          }
+          const int es = it->second;
+          const std::string pp = "p" + std::to_string(es), per = std::to_string(in.period) + "ll";
           std::string ld;
-          if (in.mode == IN_FULL) ld = "__ldg(" + pp + " + e)";
+          if (cmode[es]) ld = cached_ref(es);
+          else if (in.mode == IN_FULL) ld = "__ldg(" + pp + " + e)";
           else if (in.mode == IN_SCALAR) ld = "__ldg(" + pp + ")";
           else if (in.mode == IN_PERIOD) ld = "__ldg(" + pp + " + e % " + per + ")";
           else ld = "__ldg(" + pp + " + e / " + per + ")";
@@ -814,8 +856,38 @@ void Graph::emit_ew_group(int gi, const int* seed_ptr, float* scratch, size_t sc
     // (the unfused row kernel's order)
     const bool mean = P.kind[G.red] == "mean_last";
     k << "  const int lane = threadIdx.x & 31;\n  const i64 nw = ((i64)gridDim.x * 256) >> 5;\n";
+    // the loop over a row's elements: fully unrolled over the lane's KJ
+    // cached elements, or the plain strided loop
+    auto row_loop = [&](const char* ind) {
+      std::string s = ind;
+      if (rowc)
+        return s + "#pragma unroll\n" + s + "for (int jj = 0; jj < " + std::to_string(KJ) + "; ++jj) {\n" + s +
+               "  const i64 j = lane + 32 * jj;\n";
+      return s + "for (i64 j = lane; j < " + L + "; j += 32) {\n";
+    };
+    for (size_t si = 0; si < cmode.size(); ++si)
+      if (cmode[si] == 2)
+        k << "  float c" << si << "[" << KJ << "];\n#pragma unroll\n  for (int jj = 0; jj < " << KJ << "; ++jj) c" << si
+          << "[jj] = __ldg(p" << si << " + lane + 32 * jj);\n";
     k << "  for (i64 r = (((i64)blockIdx.x * 256 + threadIdx.x) >> 5); r < " << rows << "ll; r += nw) {\n";
-    if (G.pre >= 0) {
+    for (size_t si = 0; si < cmode.size(); ++si) {
+      if (cmode[si] == 1)
+        k << "    float c" << si << "[" << KJ << "];\n#pragma unroll\n    for (int jj = 0; jj < " << KJ << "; ++jj) c" << si
+          << "[jj] = __ldg(p" << si << " + r * " << L << " + lane + 32 * jj);\n";
+      if (cmode[si] == 3) k << "    const float s" << si << " = __ldg(p" << si << " + r);\n";
+    }
+    if (G.pre >= 0 && rowc) {
+      const int b = P.out[G.pre];
+      k << "    float accp = 0.f;\n" << row_loop("    ") << "      accp += "
+        << (cmode[pre_slot] ? cached_ref(pre_slot) : "__ldg(p" + std::to_string(pre_slot) + " + r * " + L + " + j)")
+        << ";\n    }\n";
+      k << "    for (int o = 16; o > 0; o >>= 1) accp += __shfl_xor_sync(0xffffffffu, accp, o);\n";
+      k << "    const float v" << b << " = "
+        << (P.kind[G.pre] == "mean_last" ? "__fdiv_rn(accp, " + lit((float)len) + ")" : "accp") << ";\n";
+      for (int y : pre_vals)
+        if (y != b) k << "    const float v" << y << " = v" << b << ";\n";
+      k << "    if (lane == 0) outp[r] = v" << b << ";\n";
+    } else if (G.pre >= 0) {
       // first pass: the absorbed row reduction, in the same lane order and
       // tree as the row kernels; lane 0 stores it, every lane keeps it
       const int b = P.out[G.pre];
@@ -828,8 +900,10 @@ void Graph::emit_ew_group(int gi, const int* seed_ptr, float* scratch, size_t sc
         if (y != b) k << "    const float v" << y << " = v" << b << ";\n";
       k << "    if (lane == 0) outp[r] = v" << b << ";\n";
     }
-    k << "    float acc = 0.f;\n#pragma unroll 4\n    for (i64 j = lane; j < " << L << "; j += 32) {\n      const i64 e = r * " << L
-      << " + j;\n";
+    if (rowc) k << "    float acc = 0.f;\n" << row_loop("    ") << "      const i64 e = r * " << L << " + j;\n";
+    else
+      k << "    float acc = 0.f;\n#pragma unroll 4\n    for (i64 j = lane; j < " << L << "; j += 32) {\n      const i64 e = r * " << L
+        << " + j;\n";
     k << lane.str() << ops.str() << "      acc += " << value << ";\n    }\n";
     k << "    for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);\n";
     const std::string red = mean ? "__fdiv_rn(acc, " + lit((float)len) + ")" : "acc";
@@ -839,8 +913,7 @@ void Graph::emit_ew_group(int gi, const int* seed_ptr, float* scratch, size_t sc
       k << "    {\n      const float v" << P.out[G.red] << " = " << red << ";\n" << post.str();
       k << "      if (lane == 0) {\n        out[r] = v" << P.out[G.red] << ";\n" << post_w.str() << "      }\n";
       if (has_epi)
-        k << "      for (i64 j = lane; j < " << L << "; j += 32) {\n        const i64 e = r * " << L << " + j;\n"
-          << epi.str() << "      }\n";
+        k << row_loop("      ") << "        const i64 e = r * " << L << " + j;\n" << epi.str() << "      }\n";
       k << "    }\n  }\n}\n";
     } else {
       k << "    if (lane == 0) out[r] = " << red << ";\n  }\n}\n";
