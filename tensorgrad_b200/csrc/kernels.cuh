@@ -161,6 +161,9 @@ void launch_attn_bwd(const AttnParams& P, cudaStream_t s);
 void launch_pad_rows(const float* src, int64_t ld_src, float* dst, int64_t ld_dst, int64_t rows, int64_t cols,
                      cudaStream_t s);
 void launch_fill(void* out, int64_t n, uint32_t bits, cudaStream_t s);
+// One thread that waits ns nanoseconds of GPU time (%globaltimer) and exits:
+// holds the stream while the host enqueues a profiled step behind it.
+void launch_gpu_delay(uint64_t ns, cudaStream_t s);
 void launch_arange(void* out, int64_t n, int dtype, cudaStream_t s);
 void launch_one_hot(const int* idx, void* out, int64_t n_idx, int64_t depth, int dtype, cudaStream_t s);
 void launch_randn(float* out, int64_t n, const int* seed, uint32_t salt_const, cudaStream_t s);

@@ -105,6 +105,16 @@ void launch_randn(float* out, int64_t n, const int* seed, uint32_t salt_const, c
   randn_kernel<<<grid_for(n), 256, 0, s>>>(out, n, seed, salt_const);
 }
 
+__global__ void gpu_delay_kernel(uint64_t ns) {
+  uint64_t t0, t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t0));
+  do {
+    __nanosleep(2000);
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  } while (t - t0 < ns);
+}
+void launch_gpu_delay(uint64_t ns, cudaStream_t s) { gpu_delay_kernel<<<1, 1, 0, s>>>(ns); }
+
 // ------------------------------------------------------------ embeddings --
 // Gather rows: replaces the reference's oneHot(idx) @ table contraction
 // (src/ops.ts:626-635) with a row copy; float4 when D % 4 == 0.
@@ -129,8 +139,25 @@ __global__ void __launch_bounds__(256) gather_rows_kernel(const int* __restrict_
     }
   }
 }
+// Rows of D % 4 == 0 and D <= 1024: a warp per row, lanes over the row's
+// float4s (no 64-bit division per element), 8 rows per block.
+__global__ void __launch_bounds__(256) gather_rows4_kernel(const int* __restrict__ idx, const float* __restrict__ table,
+                                                           float* __restrict__ out, int64_t rows, int64_t V, int D4) {
+  const int lane = threadIdx.x & 31;
+  for (int64_t r = ((int64_t)blockIdx.x * 256 + threadIdx.x) >> 5; r < rows; r += ((int64_t)gridDim.x * 256) >> 5) {
+    const int64_t v = __ldg(idx + r);
+    const bool ok = v >= 0 && v < V;
+    const float4* src = reinterpret_cast<const float4*>(table + (ok ? v : 0) * D4 * 4);
+    float4* dst = reinterpret_cast<float4*>(out + r * D4 * 4);
+    for (int c = lane; c < D4; c += 32) dst[c] = ok ? __ldg(src + c) : make_float4(0.f, 0.f, 0.f, 0.f);
+  }
+}
 void launch_gather_rows(const int* idx, const float* table, float* out, int64_t rows, int64_t V, int64_t D,
                         cudaStream_t s) {
+  if ((D & 3) == 0 && D <= 4096 && ((uintptr_t)table & 15) == 0 && ((uintptr_t)out & 15) == 0) {
+    gather_rows4_kernel<<<grid_for(rows * 32), 256, 0, s>>>(idx, table, out, rows, V, (int)(D >> 2));
+    return;
+  }
   gather_rows_kernel<<<grid_for(rows * D / ((D & 3) == 0 ? 4 : 1)), 256, 0, s>>>(idx, table, out, rows, V, D);
 }
 
@@ -235,6 +262,39 @@ __global__ void __launch_bounds__(256) emb_sum_kernel(const int* __restrict__ st
     }
   }
 }
+// D % 4 == 0: one warp per (vocabulary row, 128 columns), four columns per
+// lane, rows of the bucket in ascending order as above (the same sums, bit
+// for bit), eight rows' loads issued before their adds.
+__global__ void __launch_bounds__(256) emb_sum4_kernel(const int* __restrict__ start, const int* __restrict__ perm,
+                                                       const float* __restrict__ dy, float* __restrict__ dtable,
+                                                       int64_t V, int D4) {
+  const int lane = threadIdx.x & 31;
+  const int cb = (D4 + 31) / 32;
+  const int64_t units = V * cb;
+  for (int64_t u = ((int64_t)blockIdx.x * 256 + threadIdx.x) >> 5; u < units; u += ((int64_t)gridDim.x * 256) >> 5) {
+    const int64_t v = u / cb;
+    const int c = (int)(u % cb) * 32 + lane;
+    const int s0 = __ldg(start + v), s1 = __ldg(start + v + 1);
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (c < D4) {
+      const float4* src = reinterpret_cast<const float4*>(dy) + c;
+      int k = s0;
+      for (; k + 8 <= s1; k += 8) {
+        float4 x[8];
+#pragma unroll
+        for (int q = 0; q < 8; ++q) x[q] = __ldg(src + (int64_t)__ldg(perm + k + q) * D4);
+#pragma unroll
+        for (int q = 0; q < 8; ++q) { acc.x += x[q].x; acc.y += x[q].y; acc.z += x[q].z; acc.w += x[q].w; }
+      }
+      for (; k < s1; ++k) {
+        const float4 x = __ldg(src + (int64_t)__ldg(perm + k) * D4);
+        acc.x += x.x; acc.y += x.y; acc.z += x.z; acc.w += x.w;
+      }
+      reinterpret_cast<float4*>(dtable + v * D4 * 4)[c] = acc;
+    }
+  }
+}
+
 void launch_embedding_grad(const int* idx, const float* dy, float* dtable, int64_t rows, int64_t V, int64_t D,
                            int* scratch, cudaStream_t s) {
   int64_t nchunk = emb_chunks(rows);
@@ -246,6 +306,11 @@ void launch_embedding_grad(const int* idx, const float* dy, float* dtable, int64
   emb_bucket_kernel<<<(unsigned)((V + 255) / 256), 256, 0, s>>>(cnt, start, nchunk, V);
   emb_scan_kernel<<<1, 1024, 0, s>>>(start, V);
   if (nchunk > 0) emb_place_kernel<<<(unsigned)nchunk, 32, 0, s>>>(idx, cnt, start, perm, rows, V);
+  if ((D & 3) == 0 && ((uintptr_t)dy & 15) == 0 && ((uintptr_t)dtable & 15) == 0) {
+    const int64_t units = V * ((D / 4 + 31) / 32);
+    emb_sum4_kernel<<<grid_for(units * 32), 256, 0, s>>>(start, perm, dy, dtable, V, (int)(D / 4));
+    return;
+  }
   int64_t cap = (int64_t)device_sm_count() * 16;
   int64_t blocks = V < cap ? V : cap;
   emb_sum_kernel<<<(unsigned)(blocks < 1 ? 1 : blocks), 256, 0, s>>>(start, perm, dy, dtable, V, D);

@@ -392,11 +392,13 @@ int64_t colsum_col_blocks(int64_t inner, bool vec) {
   return (cols + 31) / 32;
 }
 
-// Row chunks: about four blocks per SM, at least 64 rows per chunk.
+// Row chunks: at most eight blocks per SM in one wave (column blocks x
+// chunks <= 8 x SMs, so no partial second wave), at least 64 rows per chunk.
+// Hence chunks x columns <= 8 x SMs x 128 whenever there is more than one.
 int64_t colsum_chunks(int64_t outer, int64_t inner) {
   const int64_t sms = device_sm_count();
   const int64_t cb = colsum_col_blocks(inner, inner % 4 == 0);
-  const int64_t want = (4 * sms + cb - 1) / cb;
+  const int64_t want = (8 * sms) / cb;
   const int64_t maxc = (outer + 63) / 64;
   const int64_t c = want < maxc ? want : maxc;
   return c < 1 ? 1 : c;
@@ -420,7 +422,7 @@ __global__ void __launch_bounds__(256) colsum_partial_kernel(const float* __rest
 #pragma unroll
   for (int l = 0; l < W; ++l) acc[l] = 0.f;
   if (col < inner) {
-#pragma unroll 4
+#pragma unroll 8
     for (int64_t r = r0 + ty; r < r1; r += 8) {
       if constexpr (VEC) {
         const float4 v = __ldg(reinterpret_cast<const float4*>(x + r * inner + col));

@@ -1420,10 +1420,42 @@ void Graph::profile_step(std::vector<float>& ms) {
   host_scalars();
   std::vector<cudaEvent_t> ev(launches_.size() + 1);
   for (auto& x : ev) TG_CUDA(cudaEventCreate(&x));
-  TG_CUDA(cudaEventRecord(ev[0], s));
-  for (size_t i = 0; i < launches_.size(); ++i) {
-    launches_[i](s);
-    TG_CUDA(cudaEventRecord(ev[i + 1], s));
+  // The launches and an event record node after each run as one CUDA graph,
+  // as the step itself does, so each interval is the kernel plus the graph's
+  // own node-to-node latency rather than the host's launch rate.
+  bool graphed = false;
+  if (use_graph_ && cudaStreamBeginCapture(s, cudaStreamCaptureModeThreadLocal) == cudaSuccess) {
+    cudaGraph_t g = nullptr;
+    cudaGraphExec_t gx = nullptr;
+    bool ok = cudaEventRecordWithFlags(ev[0], s, cudaEventRecordExternal) == cudaSuccess;
+    try {
+      for (size_t i = 0; ok && i < launches_.size(); ++i) {
+        launches_[i](s);
+        ok = cudaEventRecordWithFlags(ev[i + 1], s, cudaEventRecordExternal) == cudaSuccess;
+      }
+    } catch (...) {
+      ok = false;
+    }
+    ok = cudaStreamEndCapture(s, &g) == cudaSuccess && ok;
+    if (ok && cudaGraphInstantiate(&gx, g, 0) == cudaSuccess) {
+      graphed = cudaGraphLaunch(gx, s) == cudaSuccess;
+      TG_CUDA(cudaStreamSynchronize(s));
+      cudaGraphExecDestroy(gx);
+    }
+    if (g) cudaGraphDestroy(g);
+    cudaGetLastError();
+  }
+  if (!graphed) {
+    // eager fallback: the GPU waits while the host enqueues every launch and
+    // event, so the events time the kernels back to back
+    const uint64_t hold_ns =
+        std::min<uint64_t>(200000000ull, std::max<uint64_t>(5000000ull, 20000ull * launches_.size()));
+    launch_gpu_delay(hold_ns, s);
+    TG_CUDA(cudaEventRecord(ev[0], s));
+    for (size_t i = 0; i < launches_.size(); ++i) {
+      launches_[i](s);
+      TG_CUDA(cudaEventRecord(ev[i + 1], s));
+    }
   }
   TG_CUDA(cudaStreamSynchronize(s));
   TG_CUDA(cudaGetLastError());

@@ -934,7 +934,7 @@ void Graph::emit_ew_group(int gi, const int* seed_ptr, float* scratch, size_t sc
     k << "  const i64 r0 = (i64)blockIdx.y * " << rp << "ll;\n";
     k << "  const i64 r1 = r0 + " << rp << "ll < " << rows << "ll ? r0 + " << rp << "ll : " << rows << "ll;\n";
     k << "  float acc[" << W << "];\n  for (int l = 0; l < " << W << "; ++l) acc[l] = 0.f;\n";
-    k << "  if (col < " << L << ") {\n#pragma unroll 2\n    for (i64 r = r0 + ty; r < r1; r += 8) {\n";
+    k << "  if (col < " << L << ") {\n#pragma unroll 4\n    for (i64 r = r0 + ty; r < r1; r += 8) {\n";
     if (vec) {
       k << "    const i64 i = r * " << L << " + col;\n" << pre.str();
       if (G.wt >= 0) k << "    float w4[4];\n";

@@ -45,10 +45,10 @@ def test_colsum_noalloc_matches_regular_path(ctx):
 
 
 def test_colsum_noalloc_extreme_shapes(ctx):
-    """The chunking bounds the partial sums: chunks x columns <= 4 x SMs x 128
-    + columns, which stays under the fixed array for up to 256 SMs. Very wide
-    rows, very long columns and the worst case on 148 SMs ([128, 75648]: two
-    chunks of 75648 columns, 151296 partial sums) match the regular path."""
+    """The chunking bounds the partial sums: chunks x columns <= 8 x SMs x 128,
+    which stays under the fixed array for up to 256 SMs. Very wide rows, very
+    long columns and a near-worst case on 148 SMs ([128, 75648]: two chunks of
+    75648 columns, 151296 partial sums) match the regular path."""
     import torch
     lib = BK.load()
     for outer, inner, seed in [(64, 140000, 52), (200000, 3, 53), (128, 75648, 54)]:
