@@ -236,14 +236,11 @@ def main():
 
     rank, world, local = dist_env()
     torch.cuda.set_device(local)
-    nccl_id = None
     if world > 1:
-        import torch.distributed as dist
-        dist.init_process_group("gloo")
-        obj = [BK.nccl_unique_id() if rank == 0 else None]
-        dist.broadcast_object_list(obj, src=0)
-        nccl_id = obj[0]
-    ctx = BK.Context(local, rank, world, nccl_id)
+        from tensorgrad_b200.dist import init_data_parallel
+        ctx, _group = init_data_parallel(local)
+    else:
+        ctx = BK.Context(local, rank, world, None)
     # weak scaling: a fixed batch per rank. c5 names its global batch at 8 GPUs
     # (256 = 32 per GPU), so its per-rank batch is 32 unless --batch says otherwise
     per_rank = 32 if args.config == "c5" and not args.batch else w.global_batch

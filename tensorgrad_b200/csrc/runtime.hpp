@@ -255,6 +255,12 @@ class Graph {
   bool arena_owned_[AR_COUNT] = {};
   int64_t scratch_bytes_ = 0;
   std::map<std::string, int64_t> param_off_;   // byte offset in the param arena (or parent's)
+  // Data parallel: each gradient written in place, with the index of the last
+  // op before the optimizer section that touches it (its allreduce can start
+  // after that op's launches); and the events that fork the gradient buckets
+  // onto the communication stream and join them back.
+  std::vector<std::pair<std::string, int>> grad_ready_;
+  std::vector<cudaEvent_t> dp_events_;
   std::map<std::string, int64_t> param_n_;
   std::vector<std::pair<std::string, int>> layout_;  // flat arena order (name, numel)
   int64_t flat_floats_ = 0;  // padded total floats of the flat arenas
@@ -298,9 +304,22 @@ class Context {
   int device, rank, world;
   bool dry = false;
   cudaStream_t stream = nullptr;
+  cudaStream_t comm_stream = nullptr;  // gradient allreduce buckets (world > 1)
   void* nccl = nullptr;  // ncclComm_t
+  bool nccl_aborted = false;  // set after ncclCommAbort: every later step fails with NcclError
+  int64_t dp_syncs = 0;       // completed data-parallel step waits (fault-injection counter)
   std::map<int, std::unique_ptr<Graph>> graphs;
+  // Waits for the stream. With a communicator the wait polls: a CUDA error,
+  // an asynchronous NCCL error, or no completion within TG_NCCL_TIMEOUT_S
+  // aborts the communicator and throws NcclError, so a rank whose peer
+  // stalled or left fails its step instead of hanging (the reference's
+  // worker rejects every pending request when the worker dies).
+  void sync(cudaStream_t s);
+  void check_comm() const;  // throws NcclError once the communicator was aborted
+  void abort_comm(const std::string& why);
   void allreduce_sum(float* buf, int64_t n, cudaStream_t s);
+  // In-place sum allreduce of several ranges as one NCCL group.
+  void allreduce_ranges(const std::vector<std::pair<float*, int64_t>>& ranges, cudaStream_t s);
 };
 
 }  // namespace tg

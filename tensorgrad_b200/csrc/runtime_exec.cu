@@ -6,7 +6,9 @@
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
+#include <chrono>
 #include <set>
+#include <thread>
 
 #include "runtime.hpp"
 
@@ -63,6 +65,7 @@ Graph::Graph(Context* c, int gid, Graph* par, const char* json, size_t len) : id
 }
 
 Graph::~Graph() {
+  for (auto e : dp_events_) cudaEventDestroy(e);
   if (cexec_) cudaGraphExecDestroy(cexec_);
   if (cgraph_) cudaGraphDestroy(cgraph_);
   for (int a = 0; a < AR_COUNT; ++a)
@@ -206,11 +209,18 @@ void Graph::plan_storage() {
 
   // Which roots are read or written by remaining launches.
   std::vector<int> used(nT, 0), def(nT, -1), end(nT, -1);
+  // end[] restricted to ops before the optimizer section (gradient readiness)
+  std::vector<int> end_bwd(nT, -1);
+  const int opt_stop = P.opt_start >= 0 ? P.opt_start : nO;
+  auto bump_end = [&](int r, int i) {
+    end[r] = std::max(end[r], i);
+    if (i < opt_stop) end_bwd[r] = std::max(end_bwd[r], i);
+  };
   auto touch = [&](int t, int i) {
     const TView& v = views_[t];
     int r = v.onehot ? views_[v.onehot_idx].root : v.root;
     used[r] = 1;
-    end[r] = std::max(end[r], i);
+    bump_end(r, i);
   };
   for (int i = 0; i < nO; ++i) {
     if (op_done_[i]) continue;
@@ -223,7 +233,7 @@ void Graph::plan_storage() {
         const int r = views_[w].root;
         used[r] = 1;
         if (def[r] < 0 || i < def[r]) def[r] = i;
-        end[r] = std::max(end[r], i);
+        bump_end(r, i);
       }
       for (int t : fio->second.first) touch(t, i);
       continue;
@@ -235,7 +245,7 @@ void Graph::plan_storage() {
       const int r = views_[o].root;
       used[r] = 1;
       if (def[r] < 0 || i < def[r]) def[r] = i;
-      end[r] = std::max(end[r], i);
+      bump_end(r, i);
     }
     if (action_[i] == 103) {  // row hit: reads g and the one-hot's indices
       const int m = P.producer[P.op(i)["a"].i32()];
@@ -247,7 +257,7 @@ void Graph::plan_storage() {
       const int r = views_[o].root;
       used[r] = 1;
       if (def[r] < 0 || i < def[r]) def[r] = i;
-      end[r] = std::max(end[r], i);
+      bump_end(r, i);
       continue;
     }
     if (action_[i] == 102) {  // pick: reads x and the one-hot's indices
@@ -276,14 +286,14 @@ void Graph::plan_storage() {
         const int r = views_[P.out[pr]].root;
         used[r] = 1;
         if (def[r] < 0 || i < def[r]) def[r] = i;
-        end[r] = std::max(end[r], i);
+        bump_end(r, i);
       }
       if (G.pre >= 0) touch(P.op(G.pre)["a"].i32(), i);  // the absorbed first-pass reduction's input
       if (G.epi_root >= 0) {  // and the epilogue group's result
         const int r = views_[P.out[G.epi_root]].root;
         used[r] = 1;
         if (def[r] < 0 || i < def[r]) def[r] = i;
-        end[r] = std::max(end[r], i);
+        bump_end(r, i);
         for (int m : G.epi)
           for (int t : P.op_inputs[m])
             if (!ew_internal(t)) touch(t, i);
@@ -302,7 +312,7 @@ void Graph::plan_storage() {
         const int r = views_[t].root;
         used[r] = 1;
         if (def[r] < 0 || i < def[r]) def[r] = i;
-        end[r] = std::max(end[r], i);
+        bump_end(r, i);
       }
   }
   for (int t : pinned) used[t] = 1;
@@ -324,6 +334,7 @@ void Graph::plan_storage() {
   const bool flat_m = adam_fused_ || (sgd_fused_ && sgd_.momentum > 0);
   std::set<int> grad_placed;
   grad_copy_.clear();
+  grad_ready_.clear();
   for (int i = 0; i < nO; ++i) {
     const std::string& k = P.kind[i];
     int t = P.out[i];
@@ -361,7 +372,9 @@ void Graph::plan_storage() {
     if (direct) {
       place(R, AR_GRAD, off);
       grad_placed.insert(R);
+      grad_ready_.push_back({g.first, std::max(end_bwd[R], def[R])});
     } else {
+      grad_ready_.push_back({g.first, opt_stop});
       grad_copy_.push_back({G, off});
       int r = views_[G].onehot ? views_[views_[G].onehot_idx].root : views_[G].root;
       pinned.insert(r);
@@ -623,7 +636,70 @@ void Graph::emit_launches() {
   };
 
   const bool dp = ctx->world > 1 && !parent && (adam_fused_ || sgd_fused_);
+  // Data parallel: gradient buckets. Once the ops that last touch a group of
+  // gradients (in backward order) have been emitted and the group holds
+  // DP_BUCKET_BYTES, a launch forks the communication stream off the step's
+  // stream and allreduces those ranges there, overlapping the rest of the
+  // backward pass; the optimizer section starts after a join. Every rank
+  // plans the same launch list, so the collectives are issued in the same
+  // order everywhere.
+  static const int64_t DP_BUCKET_BYTES = [] {
+    const char* e = getenv("TG_DP_BUCKET_MB");  // bucket size override (tests, tuning)
+    return e ? std::max<int64_t>(256, (int64_t)(atof(e) * 1048576.0)) : (int64_t)(24ll << 20);
+  }();
+  std::vector<std::pair<int, int64_t>> dp_order;  // (ready op, byte offset) per gradient
+  std::map<int64_t, int64_t> dp_bytes;            // byte offset -> padded bytes
+  if (dp) {
+    std::map<std::string, int> grad_of;
+    for (auto& g : P.grads) grad_of[g.first] = g.second;
+    for (auto& gr : grad_ready_) {
+      const int64_t off = param_off_.at(gr.first);
+      dp_order.push_back({gr.second, off});
+      const int G = grad_of.at(gr.first);
+      dp_bytes[off] = (P.T[G].numel + 63) / 64 * 64 * 4;
+    }
+    std::sort(dp_order.begin(), dp_order.end());
+    for (auto e : dp_events_) cudaEventDestroy(e);
+    dp_events_.clear();
+  }
+  size_t dp_next = 0;
+  std::vector<int64_t> dp_pending;
+  int64_t dp_pending_bytes = 0;
+  auto dp_flush = [&]() {
+    if (dp_pending.empty()) return;
+    std::sort(dp_pending.begin(), dp_pending.end());
+    std::vector<std::pair<float*, int64_t>> ranges;  // merged adjacent ranges, in floats
+    for (int64_t off : dp_pending) {
+      float* p = reinterpret_cast<float*>(reinterpret_cast<char*>(arena_[AR_GRAD]) + off);
+      const int64_t n = dp_bytes[off] / 4;
+      if (!ranges.empty() && ranges.back().first + ranges.back().second == p) ranges.back().second += n;
+      else ranges.push_back({p, n});
+    }
+    dp_pending.clear();
+    dp_pending_bytes = 0;
+    cudaEvent_t ev = nullptr;
+    if (!ctx->dry) TG_CUDA(cudaEventCreateWithFlags(&ev, cudaEventDisableTiming));
+    dp_events_.push_back(ev);
+    Context* c = ctx;
+    int64_t tot = 0;
+    for (auto& r : ranges) tot += r.second;
+    add("nccl_allreduce|bucket floats=" + std::to_string(tot) + " ranges=" + std::to_string(ranges.size()),
+        [c, ev, ranges](cudaStream_t s) {
+          TG_CUDA(cudaEventRecord(ev, s));
+          TG_CUDA(cudaStreamWaitEvent(c->comm_stream, ev, 0));
+          c->allreduce_ranges(ranges, c->comm_stream);
+        });
+  };
+  auto dp_collect = [&](int upto, bool all) {
+    while (dp_next < dp_order.size() && (all || dp_order[dp_next].first < upto)) {
+      dp_pending.push_back(dp_order[dp_next].second);
+      dp_pending_bytes += dp_bytes[dp_order[dp_next].second];
+      ++dp_next;
+    }
+    if (dp_pending_bytes >= DP_BUCKET_BYTES || all) dp_flush();
+  };
   for (int i = 0; i <= nO; ++i) {
+    if (dp && i < P.opt_start) dp_collect(i, false);
     if (i == P.opt_start && !parent && !P.grads.empty()) {
       for (auto& gc : grad_copy_) {
         int G = gc.first;
@@ -633,10 +709,15 @@ void Graph::emit_launches() {
         emit_copy(G, 0, dims, views_[G].strides, dst, cstrides(dims), "grad_copy");
       }
       if (dp) {
-        float* g = reinterpret_cast<float*>(arena_[AR_GRAD]);
-        int64_t n = flat_floats_;
+        dp_collect(i, true);
+        cudaEvent_t join = nullptr;
+        if (!ctx->dry) TG_CUDA(cudaEventCreateWithFlags(&join, cudaEventDisableTiming));
+        dp_events_.push_back(join);
         Context* c = ctx;
-        add("nccl_allreduce", [c, g, n](cudaStream_t s) { c->allreduce_sum(g, n, s); });
+        add("nccl_join", [c, join](cudaStream_t s) {
+          TG_CUDA(cudaEventRecord(join, c->comm_stream));
+          TG_CUDA(cudaStreamWaitEvent(s, join, 0));
+        });
       }
     }
     if (i == nO) break;
@@ -1243,6 +1324,7 @@ void Graph::host_scalars() {
 
 void Graph::launch_step() {
   cudaStream_t s = ctx->stream;
+  ctx->check_comm();
   host_scalars();
   if (use_graph_) {
     if (!captured_) {
@@ -1271,7 +1353,8 @@ void Graph::read_loss(float* out) {
                         ? reinterpret_cast<char*>(arena_[AR_PERSIST]) + loss_avg_off_
                         : ptr(P.loss);
   TG_CUDA(cudaMemcpyAsync(loss_host_, src, 4, cudaMemcpyDeviceToHost, s));
-  TG_CUDA(cudaStreamSynchronize(s));
+  if (parent) TG_CUDA(cudaStreamSynchronize(s));
+  else ctx->sync(s);
   TG_CUDA(cudaGetLastError());
   *out = loss_host_[0];
 }
@@ -1488,17 +1571,84 @@ std::string Graph::info_json() const {
 }
 
 // ---------------------------------------------------------------- Context --
+// Collective failure handling (data parallel only).
+//
+// TG_NCCL_TIMEOUT_S (default 300) bounds communicator set-up and every step's
+// completion wait. TG_FAULT injects failures on the host, faking the result
+// of the call that fails rather than breaking anything on the GPU:
+//   nccl_init        communicator set-up reports an error;
+//   nccl_init_stall  set-up never completes (the deadline and abort path runs);
+//   step_error:N     the N-th step's completion check reports an NCCL error;
+//   step_stall:N     the N-th step's completion is never observed (deadline).
+// The first two act before any CUDA call, so they also run on machines
+// without a GPU.
+static double nccl_timeout_s() {
+  const char* e = getenv("TG_NCCL_TIMEOUT_S");
+  const double v = e ? atof(e) : 300.0;
+  return v > 0 ? v : 300.0;
+}
+static std::string tg_fault() {
+  const char* e = getenv("TG_FAULT");
+  return e ? std::string(e) : std::string();
+}
+// The step number N of a "name:N" fault, or -1.
+static int64_t fault_step(const std::string& f, const char* name) {
+  const std::string p = std::string(name) + ":";
+  return f.rfind(p, 0) == 0 ? atoll(f.c_str() + p.size()) : -1;
+}
+// Polls until poll() returns 0 (done) or -1 (failed), or the deadline passes;
+// returns 0, -1, or 1 (timed out).
+template <class Poll>
+static int poll_until(double timeout_s, Poll poll) {
+  const auto t0 = std::chrono::steady_clock::now();
+  for (int it = 0;; ++it) {
+    const int r = poll();
+    if (r <= 0) return r;
+    if (std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count() > timeout_s) return 1;
+    std::this_thread::sleep_for(std::chrono::microseconds(it < 64 ? 2 : 50));
+  }
+}
+
 Context::Context(int dev, int rk, int wd, const unsigned char* nccl_id) : device(dev), rank(rk), world(wd) {
+  const std::string fault = world > 1 ? tg_fault() : std::string();
+  if (fault == "nccl_init")
+    throw TgError("NcclError", "ncclCommInitRankConfig: injected failure (TG_FAULT=nccl_init)");
+  if (fault == "nccl_init_stall") {
+    const double to = nccl_timeout_s();
+    poll_until(to, [] { return 1; });  // set-up that never completes
+    throw TgError("NcclError", "communicator set-up did not complete within " + std::to_string(to) +
+                                   " s (TG_FAULT=nccl_init_stall); communicator aborted");
+  }
   TG_CUDA(cudaSetDevice(dev));
   TG_CUDA(cudaStreamCreateWithFlags(&stream, cudaStreamNonBlocking));
   if (world > 1) {
     if (!nccl_id) throw TgError("NcclError", "world > 1 needs an NCCL unique id");
     ncclUniqueId id;
     memcpy(&id, nccl_id, sizeof(id));
-    ncclComm_t comm;
-    ncclResult_t r = ncclCommInitRank(&comm, world, id, rank);
-    if (r != ncclSuccess) throw TgError("NcclError", std::string("ncclCommInitRank: ") + ncclGetErrorString(r));
+    ncclComm_t comm = nullptr;
+    // Non-blocking set-up, polled against the deadline: a peer that never
+    // joins ends in ncclCommAbort and an NcclError instead of a hang.
+    ncclConfig_t cfg = NCCL_CONFIG_INITIALIZER;
+    cfg.blocking = 0;
+    ncclResult_t r = ncclCommInitRankConfig(&comm, world, id, rank, &cfg);
+    if (r != ncclSuccess && r != ncclInProgress)
+      throw TgError("NcclError", std::string("ncclCommInitRankConfig: ") + ncclGetErrorString(r));
+    ncclResult_t st = ncclInProgress;
+    const double to = nccl_timeout_s();
+    const int w = poll_until(to, [&] {
+      if (ncclCommGetAsyncError(comm, &st) != ncclSuccess) return -1;
+      return st == ncclInProgress ? 1 : (st == ncclSuccess ? 0 : -1);
+    });
+    if (w != 0) {
+      ncclCommAbort(comm);
+      throw TgError("NcclError", w > 0 ? "communicator set-up did not complete within " + std::to_string(to) +
+                                             " s (a peer rank never joined); communicator aborted"
+                                       : std::string("communicator set-up failed: ") + ncclGetErrorString(st));
+    }
     nccl = comm;
+    int lo = 0, hi = 0;
+    TG_CUDA(cudaDeviceGetStreamPriorityRange(&lo, &hi));
+    TG_CUDA(cudaStreamCreateWithPriority(&comm_stream, cudaStreamNonBlocking, hi));
   }
 }
 
@@ -1506,13 +1656,93 @@ Context::Context(Dry, int wd) : device(-1), rank(0), world(wd), dry(true) {}
 
 Context::~Context() {
   graphs.clear();
-  if (nccl) ncclCommDestroy(reinterpret_cast<ncclComm_t>(nccl));
+  if (nccl && !nccl_aborted) ncclCommDestroy(reinterpret_cast<ncclComm_t>(nccl));
+  if (comm_stream) cudaStreamDestroy(comm_stream);
   if (stream) cudaStreamDestroy(stream);
 }
 
+// On a non-blocking communicator a call may return ncclInProgress; its
+// enqueue is complete once ncclCommGetAsyncError stops reporting that, and
+// the next NCCL call (or the end of a stream capture) must wait for it.
+static ncclResult_t settle(ncclComm_t comm, ncclResult_t r) {
+  if (r != ncclInProgress) return r;
+  ncclResult_t st = ncclInProgress;
+  const int w = poll_until(nccl_timeout_s(), [&] {
+    if (ncclCommGetAsyncError(comm, &st) != ncclSuccess) return -1;
+    return st == ncclInProgress ? 1 : 0;
+  });
+  return w == 0 ? st : ncclInternalError;
+}
+
+void Context::check_comm() const {
+  if (nccl_aborted) throw TgError("NcclError", "the communicator was aborted after an earlier collective failure");
+}
+
+void Context::abort_comm(const std::string& why) {
+  if (nccl && !nccl_aborted) ncclCommAbort(reinterpret_cast<ncclComm_t>(nccl));
+  nccl_aborted = true;
+  throw TgError("NcclError", why + "; communicator aborted");
+}
+
+void Context::allreduce_ranges(const std::vector<std::pair<float*, int64_t>>& ranges, cudaStream_t s) {
+  check_comm();
+  ncclComm_t comm = reinterpret_cast<ncclComm_t>(nccl);
+  ncclResult_t r = settle(comm, ncclGroupStart());
+  for (size_t i = 0; r == ncclSuccess && i < ranges.size(); ++i)
+    r = settle(comm, ncclAllReduce(ranges[i].first, ranges[i].first, (size_t)ranges[i].second, ncclFloat32, ncclSum,
+                                   comm, s));
+  const ncclResult_t r2 = settle(comm, ncclGroupEnd());
+  if (r != ncclSuccess || r2 != ncclSuccess)
+    throw TgError("NcclError", std::string("ncclAllReduce (bucket): ") + ncclGetErrorString(r != ncclSuccess ? r : r2));
+}
+
 void Context::allreduce_sum(float* buf, int64_t n, cudaStream_t s) {
-  ncclResult_t r = ncclAllReduce(buf, buf, (size_t)n, ncclFloat32, ncclSum, reinterpret_cast<ncclComm_t>(nccl), s);
+  check_comm();
+  ncclComm_t comm = reinterpret_cast<ncclComm_t>(nccl);
+  ncclResult_t r = settle(comm, ncclAllReduce(buf, buf, (size_t)n, ncclFloat32, ncclSum, comm, s));
   if (r != ncclSuccess) throw TgError("NcclError", std::string("ncclAllReduce: ") + ncclGetErrorString(r));
+}
+
+void Context::sync(cudaStream_t s) {
+  if (!nccl) {
+    TG_CUDA(cudaStreamSynchronize(s));
+    return;
+  }
+  check_comm();
+  const int64_t n = ++dp_syncs;
+  const std::string fault = tg_fault();
+  const bool stall = fault_step(fault, "step_stall") == n, err = fault_step(fault, "step_error") == n;
+  ncclComm_t comm = reinterpret_cast<ncclComm_t>(nccl);
+  cudaError_t ce = cudaSuccess;
+  ncclResult_t st = ncclSuccess;
+  const double to = nccl_timeout_s();
+  const int w = poll_until(to, [&] {
+    ce = cudaStreamQuery(s);
+    if (ce != cudaSuccess && ce != cudaErrorNotReady) return -1;
+    if (err || ncclCommGetAsyncError(comm, &st) != ncclSuccess || (st != ncclSuccess && st != ncclInProgress)) {
+      if (err) st = ncclRemoteError;
+      ce = cudaSuccess;
+      return -1;
+    }
+    return (ce == cudaSuccess && !stall) ? 0 : 1;
+  });
+  if (w == 0) return;
+  if (ce != cudaSuccess) throw TgError("CudaError", std::string("step: ") + cudaGetErrorString(ce));
+  if (w > 0) {
+    // the step's work may still be queued behind a collective that waits on
+    // a peer: abort it, then wait for the stream to drain
+    if (!nccl_aborted) ncclCommAbort(comm);
+    nccl_aborted = true;
+    cudaStreamSynchronize(s);
+    throw TgError("NcclError", "step did not complete within " + std::to_string(to) + " s" +
+                                   (stall ? " (TG_FAULT=step_stall)" : " (a peer rank stalled or left)") +
+                                   "; communicator aborted");
+  }
+  if (!nccl_aborted) ncclCommAbort(comm);
+  nccl_aborted = true;
+  cudaStreamSynchronize(s);
+  throw TgError("NcclError", std::string("collective failed: ") + ncclGetErrorString(st) +
+                                 (err ? " (TG_FAULT=step_error)" : "") + "; communicator aborted");
 }
 
 }  // namespace tg

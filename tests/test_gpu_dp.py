@@ -57,9 +57,14 @@ def _rank(rank, port, out_path):
         dist.destroy_process_group()
 
 
-def test_two_gpu_step_matches_whole_batch(tmp_path):
+@pytest.mark.parametrize("bucket_mb", [None, "0.02"])
+def test_two_gpu_step_matches_whole_batch(tmp_path, bucket_mb, monkeypatch):
+    """bucket_mb "0.02" splits the gradient allreduce into many buckets that
+    run on the communication stream during the backward pass."""
     if torch.cuda.device_count() < WORLD:
         pytest.skip("needs two GPUs")
+    if bucket_mb:
+        monkeypatch.setenv("TG_DP_BUCKET_MB", bucket_mb)
     import torch.multiprocessing as mp
     from oracle.driver import OracleTrainer
     from tensorgrad_b200 import configs as CF
@@ -78,3 +83,58 @@ def test_two_gpu_step_matches_whole_batch(tmp_path):
     for n, g in orc.grads().items():
         # the arena holds the sum over ranks of each rank's mean gradient
         close(r[f"g_{n}"] / WORLD, np.asarray(g).reshape(r[f"g_{n}"].shape), tensor_frac=1.0)
+
+
+def _fault_rank(rank, port, fault, out_path):
+    import torch.distributed as dist
+    from tensorgrad_b200 import backend as BK
+    from tensorgrad_b200 import configs as CF
+    from tensorgrad_b200.compile import build_training_ir, initial_params
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    os.environ["TG_FAULT"] = fault
+    os.environ["TG_NCCL_TIMEOUT_S"] = "2"
+    dist.init_process_group("gloo", rank=rank, world_size=WORLD)
+    try:
+        obj = [BK.nccl_unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(obj, src=0)
+        ctx = BK.Context(rank, rank, WORLD, obj[0])
+        B = TINY["batch"]
+        w = CF.workload("c4", **TINY)
+        ir = build_training_ir(w.make_model(), w.loss, w.inputs(B), w.optimizer)
+        dg = BK.DeviceGraph(ctx, ir.program)
+        dg.upload_params(initial_params(ir.graph, ir.materialized.initFns, CF.PARAM_SEED))
+        data = CF.shard(w.data(B * WORLD), rank, WORLD)
+        out = []
+        for _ in range(3):
+            try:
+                dg.step(data)
+                out.append("ok")
+            except BK.TgError as e:
+                out.append(f"{e.name}: {e.message}")
+        if rank == 0:
+            with open(out_path, "w") as f:
+                f.write("\n".join(out))
+        dg.destroy()
+        ctx.close()
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("fault", ["step_error:2", "step_stall:2"])
+def test_two_gpu_collective_failure_aborts_the_communicator(tmp_path, fault):
+    """The completion wait of a data-parallel step fails with NcclError when
+    the communicator reports an error or the step does not complete within
+    TG_NCCL_TIMEOUT_S; the communicator is aborted and every later step fails
+    at once. The failures are injected on the host (TG_FAULT fakes the result
+    of the completion check); the collectives themselves complete on both
+    GPUs, so no device is left waiting."""
+    if torch.cuda.device_count() < WORLD:
+        pytest.skip("needs two GPUs")
+    import torch.multiprocessing as mp
+    out = str(tmp_path / "fault.txt")
+    mp.spawn(_fault_rank, args=(_free_port(), fault, out), nprocs=WORLD, join=True)
+    lines = open(out).read().split("\n")
+    assert lines[0] == "ok"
+    assert lines[1].startswith("NcclError") and "aborted" in lines[1]
+    assert lines[2].startswith("NcclError") and "aborted after an earlier collective failure" in lines[2]

@@ -329,3 +329,22 @@ def test_launch_bytes_count_each_tensor_once():
     by = dict(zip(kinds(c4), c4["launchBytes"]))
     assert by["adam_flat"] > 0 and by["colsum"] > 0 and by["gather_rows"] > 0
     assert all(b == 0 for k, b in zip(kinds(c4), c4["launchBytes"]) if k.startswith("matmul"))
+
+
+def test_data_parallel_gradients_allreduce_in_buckets_during_backward():
+    """Full C4 at world 2: the gradient allreduce is split into buckets that
+    start while backward GEMMs are still to come, cover every gradient's
+    padded range exactly once, and join before the fused optimizer."""
+    w = CF.workload("c4", batch=8)
+    ir = build_training_ir(w.make_model(), w.loss, w.inputs(8), w.optimizer)
+    r = BK.plan_dry(ir.program, world=2)
+    labels = r["launches"]
+    k = kinds(r)
+    buckets = [i for i, x in enumerate(k) if x == "nccl_allreduce"]
+    assert len(buckets) >= 2
+    floats = sum(int(labels[i].split("floats=")[1].split()[0]) for i in buckets)
+    padded = sum((int(np.prod(t.shape)) + 63) // 64 * 64 for t in ir.paramGrads.values())
+    assert floats == padded
+    last_gemm = max(i for i, x in enumerate(k) if x.startswith("matmul"))
+    assert buckets[0] < last_gemm
+    assert k.index("nccl_join") > buckets[-1] and k.index("nccl_join") < k.index("adam_flat")
