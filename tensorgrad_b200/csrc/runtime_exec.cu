@@ -66,8 +66,11 @@ Graph::Graph(Context* c, int gid, Graph* par, const char* json, size_t len) : id
 
 Graph::~Graph() {
   for (auto e : dp_events_) cudaEventDestroy(e);
-  if (cexec_) cudaGraphExecDestroy(cexec_);
-  if (cgraph_) cudaGraphDestroy(cgraph_);
+  // A captured step of an aborted communicator keeps NCCL resources that the
+  // abort already released: it is left to process exit rather than destroyed.
+  const bool keep = ctx && ctx->nccl_aborted;
+  if (cexec_ && !keep) cudaGraphExecDestroy(cexec_);
+  if (cgraph_ && !keep) cudaGraphDestroy(cgraph_);
   for (int a = 0; a < AR_COUNT; ++a)
     if (arena_owned_[a] && arena_[a]) cudaFree(arena_[a]);
   if (loss_host_) cudaFreeHost(loss_host_);
@@ -1719,12 +1722,15 @@ void Context::sync(cudaStream_t s) {
   const int w = poll_until(to, [&] {
     ce = cudaStreamQuery(s);
     if (ce != cudaSuccess && ce != cudaErrorNotReady) return -1;
-    if (err || ncclCommGetAsyncError(comm, &st) != ncclSuccess || (st != ncclSuccess && st != ncclInProgress)) {
-      if (err) st = ncclRemoteError;
+    if (ncclCommGetAsyncError(comm, &st) != ncclSuccess || (st != ncclSuccess && st != ncclInProgress)) {
       ce = cudaSuccess;
       return -1;
     }
-    return (ce == cudaSuccess && !stall) ? 0 : 1;
+    if (ce != cudaSuccess) return 1;  // still running
+    // injected faults are reported only once the step's work has finished on
+    // this device, so the abort below never cuts a collective short
+    if (err) { st = ncclRemoteError; return -1; }
+    return stall ? 1 : 0;
   });
   if (w == 0) return;
   if (ce != cudaSuccess) throw TgError("CudaError", std::string("step: ") + cudaGetErrorString(ce));
