@@ -182,6 +182,13 @@ struct GemmDesc {
   int64_t batch2;                                 // inner batch extent (1 = single batch dim)
   int64_t a_batch2, b_batch2, c_batch2;           // strides of the inner batch index
   int64_t ldc_n;                                  // C column stride (0 is read as 1)
+  // Causal structure of A (square M == K, batched attention): 1 = A(m, k) is
+  // exactly zero for k > m (a causal softmax, or a product with one), so the
+  // rows of a tile need only k below the tile's end; 2 = zero for k < m (the
+  // transpose), the rows need only k from the tile's start. 0 = dense.
+  // tri_cols: the same for B's columns (B(k, n) zero for k > n: 1; k < n: 2).
+  int tri;
+  int tri_cols;
   float* workspace;                               // split-K partial tiles (may be null)
   int64_t workspace_floats;
 };

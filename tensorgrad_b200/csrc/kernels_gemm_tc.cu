@@ -100,6 +100,8 @@ struct TcParams {
   int trace;        // record the pipeline timeline of CTA (0,0,0)
   int tma_store;    // write the tile with TMA stores through tmC (else plain stores)
   int64_t units;    // output tiles x batch x K ranges
+  int tri;          // GemmDesc::tri for the output rows (m tiles), or for the columns when
+  int tri_n;        // tri_n (the operands were swapped); only without split-K
 };
 
 // ------------------------------------------------------------- PTX helpers --
@@ -218,6 +220,11 @@ __device__ __forceinline__ TcUnit tc_unit(const TcParams& P, int64_t u) {
   const int nk_all = (int)((P.K + TC_BK - 1) / TC_BK);
   U.kbeg = U.sp * P.kps;
   U.nk = max(0, min(nk_all, U.kbeg + P.kps) - U.kbeg);
+  if (P.tri) {  // skip the K stages whose products are exactly zero (causal A)
+    const int r0 = (int)(P.tri_n ? U.n0 : U.m0);
+    if (P.tri == 1) U.nk = min(nk_all, (r0 + TC_BM + TC_BK - 1) / TC_BK);
+    else { U.kbeg = r0 / TC_BK; U.nk = max(0, nk_all - U.kbeg); }
+  }
   return U;
 }
 
@@ -738,6 +745,9 @@ bool launch_gemm_tc(const GemmDesc& g, cudaStream_t s) {
   p.ws = g.workspace;
   static const int trace = [] { const char* e = getenv("TG_GEMM_TRACE"); return e && e[0] == '1' ? 1 : 0; }();
   p.trace = trace;
+  // rows of the kernel's tiles are the problem's m tiles, or its n tiles after a swap
+  p.tri = splits == 1 ? (g.tri ? g.tri : g.tri_cols) : 0;
+  p.tri_n = g.tri ? (swap ? 1 : 0) : (swap ? 0 : 1);
   // Output tensor map (row-major tiles {32 inner, 128 outer}); plain stores
   // when C's layout is not TMA-describable or the result accumulates.
   CUtensorMap tc;

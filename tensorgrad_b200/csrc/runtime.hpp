@@ -277,7 +277,9 @@ class Graph {
   std::vector<std::string> launch_kind_;
   std::vector<double> launch_bytes_;
   double next_bytes_ = 0;  // bytes of the next add()ed launch
-  double tensor_bytes(int t) const;  std::vector<std::function<void(cudaStream_t)>> post_;  // writebacks
+  double tensor_bytes(int t) const;
+  std::map<int, bool> causal_memo_;
+  bool causal_zero(int t);  std::vector<std::function<void(cudaStream_t)>> post_;  // writebacks
   cudaGraph_t cgraph_ = nullptr;
   cudaGraphExec_t cexec_ = nullptr;
   bool use_graph_ = true;

@@ -575,6 +575,34 @@ EwInput Graph::ew_input(int t, const std::vector<int64_t>& oshape, bool& vec_ok,
   return in;
 }
 
+// Tensors that are exactly zero above the diagonal of their last two dims:
+// a causal softmax's result (the masked entries are written as 0), and
+// dropouts, scalings and same-shape products of such a tensor (0 times a
+// finite value stays 0).
+bool Graph::causal_zero(int t) {
+  auto it = causal_memo_.find(t);
+  if (it != causal_memo_.end()) return it->second;
+  causal_memo_[t] = false;
+  bool z = false;
+  const int p = P.producer[t];
+  if (p >= 0) {
+    const std::string& k = P.kind[p];
+    const auto& O = P.op(p);
+    if (k == "softmax_causal_last") z = true;
+    else if (k == "dropout" || k == "mul_scalar" ||
+             ((k == "reshape" || k == "stop_gradient") && P.T[O["a"].i32()].shape == P.T[t].shape))
+      z = causal_zero(O["a"].i32());
+    else if (k == "mul") {
+      for (const char* f : {"a", "b"}) {
+        const int x = O[f].i32();
+        if (P.T[x].shape == P.T[t].shape && causal_zero(x)) z = true;
+      }
+    }
+  }
+  causal_memo_[t] = z;
+  return z;
+}
+
 double Graph::tensor_bytes(int t) const {
   const TView& v = views_[t];
   if (v.onehot) return 4.0 * (double)P.T[v.onehot_idx].numel;  // a virtual one-hot reads its indices
@@ -1071,6 +1099,21 @@ void Graph::emit_launches() {
       }
       g.workspace = scratch;
       g.workspace_floats = (int64_t)scratch_floats;
+      // causal A: the square [.., T, T] operand of attention's P.V and of the
+      // gradient GEMMs, exactly zero above (or, transposed, below) the diagonal
+      auto square_root = [&](const TView& v, int64_t T) {
+        const auto& rs = P.T[v.root].shape;
+        const int rr = (int)rs.size();
+        return !v.onehot && v.off == 0 && rr >= 2 && rs[rr - 1] == T && rs[rr - 2] == T && causal_zero(v.root);
+      };
+      if (k == "matmul_batched" && g.M == g.K && g.M >= 256 && square_root(va, g.M)) {
+        if (g.lda_m == g.M && g.lda_k == 1) g.tri = 1;
+        else if (g.lda_m == 1 && g.lda_k == g.M) g.tri = 2;
+      }
+      if (k == "matmul_batched" && !g.tri && g.N == g.K && g.N >= 256 && square_root(vb, g.N)) {
+        if (g.ldb_k == g.N && g.ldb_n == 1) g.tri_cols = 2;       // B(k, n) = R[k][n]: zero for n > k
+        else if (g.ldb_k == 1 && g.ldb_n == g.N) g.tri_cols = 1;  // B(k, n) = R[n][k]: zero for k > n
+      }
       // TMA needs 16-byte aligned bases and row strides. An operand whose
       // outer stride is not a multiple of 4 floats (a vocabulary of 65) is
       // first copied to padded rows after the split-K workspace, so the
@@ -1096,9 +1139,9 @@ void Graph::emit_launches() {
         if (!pads.empty()) g.workspace_floats = wsf;
       }
       char label[160];
-      snprintf(label, sizeof label, "%s|M=%lld N=%lld K=%lld b=%lld A%s B%s%s", k.c_str(), (long long)g.M,
+      snprintf(label, sizeof label, "%s|M=%lld N=%lld K=%lld b=%lld A%s B%s%s%s", k.c_str(), (long long)g.M,
                (long long)g.N, (long long)g.K, (long long)g.batch, g.lda_k == 1 ? "k" : "mn",
-               g.ldb_k == 1 ? "k" : "mn", pads.empty() ? "" : " padded");
+               g.ldb_k == 1 ? "k" : "mn", pads.empty() ? "" : " padded", (g.tri || g.tri_cols) ? " causal" : "");
       add(label, [g, pads](cudaStream_t s) {
         for (const Pad& p : pads) launch_pad_rows(p.src, p.ld_src, p.dst, p.ld_dst, p.rows, p.cols, s);
         if (!launch_gemm_tc(g, s)) launch_gemm_simt(g, s);

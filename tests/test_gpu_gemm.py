@@ -11,6 +11,8 @@ from tensorgrad_b200.trace import tensor_input as T
 
 from .test_gpu_ops import rnd, run
 
+T_ = T
+
 pytestmark = pytest.mark.gpu
 
 
@@ -68,3 +70,35 @@ def test_gemm_simt_split_k_unaligned(ctx):
     x = rnd([8192, 96], 48)
     dy = rnd([8192, 65], 49)
     run(ctx, lambda: tg.matmul(tg.swapAxes(T("x", [8192, 96]), 0, 1), T("dy", [8192, 65])), {"x": x, "dy": dy})
+
+
+@pytest.mark.parametrize("T", [256, 384])
+@pytest.mark.parametrize("form", ["PV", "PtV", "XP", "XPt"])
+def test_gemm_skips_the_zero_half_of_a_causal_operand(ctx, T, form):
+    """A causal softmax's result is exactly zero above its diagonal, so a
+    batched GEMM with it as an operand skips the K stages of those products
+    (A = P: k below the tile's end; A = P^T: k from the tile's start; B = P or
+    P^T: the same for output columns). Results match the dense oracle."""
+    B_, H, d = 2, 3, 64
+    s = rnd([B_, H, T, T], 90, -3, 3)
+    v = rnd([B_, H, T, d], 91)
+    x = rnd([B_, H, d, T], 92)
+
+    def build():
+        P = tg.softmaxCausal(T_("s", [B_, H, T, T]))
+        if form == "PV":
+            return tg.matmul(P, T_("v", [B_, H, T, d]))
+        if form == "PtV":
+            return tg.matmul(tg.swapAxes(P, -1, -2), T_("v", [B_, H, T, d]))
+        if form == "XP":
+            return tg.matmul(T_("x", [B_, H, d, T]), P)
+        return tg.matmul(T_("x", [B_, H, d, T]), tg.swapAxes(P, -1, -2))
+    inputs = {"s": s, "v": v} if form in ("PV", "PtV") else {"s": s, "x": x}
+    from tensorgrad_b200.compile import _program
+    from tensorgrad_b200.trace import trace_fn
+    from tensorgrad_b200 import backend as BK
+    g = trace_fn(build)
+    labels = BK.plan_dry(_program(g, {}, [], g.outputs[0], None, len(g.ops)))["launches"]
+    assert any(l.startswith("matmul_batched") and l.endswith("causal") for l in labels), labels
+    run(ctx, build, inputs)
+

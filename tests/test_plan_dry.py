@@ -348,3 +348,14 @@ def test_data_parallel_gradients_allreduce_in_buckets_during_backward():
     last_gemm = max(i for i, x in enumerate(k) if x.startswith("matmul"))
     assert buckets[0] < last_gemm
     assert k.index("nccl_join") > buckets[-1] and k.index("nccl_join") < k.index("adam_flat")
+
+
+def test_attention_gemms_with_a_causal_operand_skip_its_zero_half():
+    """C4 unfused: of the six batched GEMMs per layer, the four whose operand
+    is the causal probabilities (or the softmax gradient, a product with
+    them) are marked causal and skip the K stages of exact-zero products."""
+    w = CF.workload("c4", batch=2)
+    ir = build_training_ir(w.make_model(), w.loss, w.inputs(2), w.optimizer)
+    labels = [x for x in BK.plan_dry(ir.program)["launches"] if x.startswith("matmul_batched")]
+    assert len(labels) == 36
+    assert sum(x.endswith(" causal") for x in labels) == 24
