@@ -45,9 +45,12 @@ class AbortError(TgError):
 
 
 def load(path: str = LIB_PATH):
+    """Loads the C ABI library (TG_LIB names another build of it, for A/B
+    measurements of build-time variants)."""
     global _lib
     if _lib is not None:
         return _lib
+    path = os.environ.get("TG_LIB", path)
     if not os.path.exists(path):
         raise BackendUnavailable(f"{path} is missing; run `python -m tensorgrad_b200.build`")
     lib = C.CDLL(path)

@@ -343,10 +343,17 @@ __global__ void __launch_bounds__(448, 1) gemm_tc_kernel(const __grid_constant__
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const bool partial = P.splits > 1;
+  // The pipeline trace exists only in builds with TG_GEMM_TRACE_BUILD
+  // defined: the MMA-issuing thread's loop is the kernel's critical path, and
+  // even an untaken branch per stage there costs throughput.
+#ifdef TG_GEMM_TRACE_BUILD
   const bool tr = P.trace && blockIdx.x == 0;
   auto mark = [&](int row, int i) {
     if (tr && i < TC_TRACE_N) g_gemm_tc_trace[row][i] = clock64();
   };
+#else
+  auto mark = [](int, int) {};
+#endif
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < NS; ++s) {
