@@ -199,7 +199,10 @@ __device__ __forceinline__ float tf32_hi(float x) { return __uint_as_float(__flo
 // accumulators every TC_CHUNK K-stages (128 MMA-K), and the epilogue warps
 // drain each finished accumulator into per-thread f32 registers with
 // round-to-nearest adds; total error then grows like sqrt(K) instead of K.
-constexpr int TC_CHUNK = 4;
+#ifndef TC_CHUNK_STAGES
+#define TC_CHUNK_STAGES 4
+#endif
+constexpr int TC_CHUNK = TC_CHUNK_STAGES;
 
 // One output tile of one batch entry and one K range: the persistent CTAs'
 // unit of work, numbered with the N tile fastest.
