@@ -209,7 +209,7 @@ void launch_gather_rows(const int* idx, const float* table, float* out, int64_t 
                         int64_t D, cudaStream_t s);
 // Deterministic embedding backward: dtable[v,:] = sum of dy[r,:] over rows r
 // with idx[r]==v, in ascending r (stable counting sort, no float atomics).
-size_t embedding_grad_scratch_ints(int64_t rows, int64_t V);
+size_t embedding_grad_scratch_ints(int64_t rows, int64_t V, int64_t D);
 void launch_embedding_grad(const int* idx, const float* dy, float* dtable, int64_t rows, int64_t V,
                            int64_t D, int* scratch, cudaStream_t s);
 // out[r] = g[r] where 0 <= t[r] < V, else 0 (the row sum of g[r] * oneHot(t)[r])

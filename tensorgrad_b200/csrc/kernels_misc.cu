@@ -6,6 +6,8 @@
 // (:212-239), max pool + grad (:1095-1185); conv2d lives in kernels_conv.cu,
 // Adam (:841-905: three kernels plus three copy-backs per param there; one
 // in-place pass over flat arenas here).
+#include <algorithm>
+
 #include "kernels.cuh"
 
 namespace tg {
@@ -167,11 +169,28 @@ void launch_gather_rows(const int* idx, const float* table, float* out, int64_t 
 // order. No float atomics, so results are bit-reproducible run to run (the
 // reference avoided atomics for the same reason, src/nn.ts:79-81).
 //
-// Scratch (ints): perm[rows] | cnt[nchunk * V] | start[V + 1].
+// Scratch (ints): perm[rows] | cnt[nchunk * V] | start[V + 1] | (256 B aligned)
+// segment partial sums (floats) [segments][V][D] when the float4 path splits
+// each bucket into segments.
 static const int64_t EMB_CHUNK = 1024;
 static int64_t emb_chunks(int64_t rows) { return (rows + EMB_CHUNK - 1) / EMB_CHUNK; }
-size_t embedding_grad_scratch_ints(int64_t rows, int64_t V) {
-  return (size_t)(rows + emb_chunks(rows) * V + V + 1);
+// Segments per bucket for the float4 sum: enough warps to keep the SMs busy
+// when the vocabulary is small (C4: 65 rows of 384 columns, about 250 rows per
+// bucket), one when it is large.
+static int64_t emb_segments(int64_t rows, int64_t V, int64_t D) {
+  if (D % 4 != 0 || V <= 0) return 1;
+  const int64_t units = V * ((D / 4 + 31) / 32);
+  const int64_t want = (int64_t)device_sm_count() * 32;
+  int64_t s = want / std::max<int64_t>(units, 1);
+  s = std::min<int64_t>(s, std::max<int64_t>(1, rows / std::max<int64_t>(V, 1) / 16));
+  return std::max<int64_t>(1, std::min<int64_t>(s, 16));
+}
+static int64_t emb_head_ints(int64_t rows, int64_t V) {
+  return (rows + emb_chunks(rows) * V + V + 1 + 63) / 64 * 64;
+}
+size_t embedding_grad_scratch_ints(int64_t rows, int64_t V, int64_t D) {
+  const int64_t s = emb_segments(rows, V, D);
+  return (size_t)(emb_head_ints(rows, V) + (s > 1 ? s * V * D : 0));
 }
 
 __global__ void emb_hist_kernel(const int* __restrict__ idx, int* __restrict__ cnt, int64_t rows, int64_t V) {
@@ -262,19 +281,25 @@ __global__ void __launch_bounds__(256) emb_sum_kernel(const int* __restrict__ st
     }
   }
 }
-// D % 4 == 0: one warp per (vocabulary row, 128 columns), four columns per
-// lane, rows of the bucket in ascending order as above (the same sums, bit
-// for bit), eight rows' loads issued before their adds.
+// D % 4 == 0: one warp per (vocabulary row, 128 columns, segment of the
+// bucket), four columns per lane, the segment's rows in ascending order,
+// eight rows' loads issued before their adds. With several segments each
+// writes a partial row and emb_fold4_kernel adds them in segment order: a
+// fixed order, so the result is deterministic.
 __global__ void __launch_bounds__(256) emb_sum4_kernel(const int* __restrict__ start, const int* __restrict__ perm,
                                                        const float* __restrict__ dy, float* __restrict__ dtable,
-                                                       int64_t V, int D4) {
+                                                       int64_t V, int D4, int nseg, float* __restrict__ part) {
   const int lane = threadIdx.x & 31;
   const int cb = (D4 + 31) / 32;
-  const int64_t units = V * cb;
+  const int64_t units = V * cb * nseg;
   for (int64_t u = ((int64_t)blockIdx.x * 256 + threadIdx.x) >> 5; u < units; u += ((int64_t)gridDim.x * 256) >> 5) {
-    const int64_t v = u / cb;
-    const int c = (int)(u % cb) * 32 + lane;
-    const int s0 = __ldg(start + v), s1 = __ldg(start + v + 1);
+    const int sg = (int)(u % nseg);
+    const int64_t vc = u / nseg;
+    const int64_t v = vc / cb;
+    const int c = (int)(vc % cb) * 32 + lane;
+    const int b0 = __ldg(start + v), b1 = __ldg(start + v + 1);
+    const int64_t len = b1 - b0;
+    const int s0 = b0 + (int)(len * sg / nseg), s1 = b0 + (int)(len * (sg + 1) / nseg);
     float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
     if (c < D4) {
       const float4* src = reinterpret_cast<const float4*>(dy) + c;
@@ -290,8 +315,21 @@ __global__ void __launch_bounds__(256) emb_sum4_kernel(const int* __restrict__ s
         const float4 x = __ldg(src + (int64_t)__ldg(perm + k) * D4);
         acc.x += x.x; acc.y += x.y; acc.z += x.z; acc.w += x.w;
       }
-      reinterpret_cast<float4*>(dtable + v * D4 * 4)[c] = acc;
+      float* dst = nseg > 1 ? part + ((int64_t)sg * V + v) * D4 * 4 : dtable + v * D4 * 4;
+      reinterpret_cast<float4*>(dst)[c] = acc;
     }
+  }
+}
+
+__global__ void __launch_bounds__(256) emb_fold4_kernel(const float* __restrict__ part, float* __restrict__ dtable,
+                                                        int64_t n4, int nseg) {
+  for (int64_t i = (int64_t)blockIdx.x * 256 + threadIdx.x; i < n4; i += (int64_t)gridDim.x * 256) {
+    float4 a = __ldg(reinterpret_cast<const float4*>(part) + i);
+    for (int sg = 1; sg < nseg; ++sg) {
+      const float4 b = __ldg(reinterpret_cast<const float4*>(part) + sg * n4 + i);
+      a.x += b.x; a.y += b.y; a.z += b.z; a.w += b.w;
+    }
+    reinterpret_cast<float4*>(dtable)[i] = a;
   }
 }
 
@@ -307,8 +345,11 @@ void launch_embedding_grad(const int* idx, const float* dy, float* dtable, int64
   emb_scan_kernel<<<1, 1024, 0, s>>>(start, V);
   if (nchunk > 0) emb_place_kernel<<<(unsigned)nchunk, 32, 0, s>>>(idx, cnt, start, perm, rows, V);
   if ((D & 3) == 0 && ((uintptr_t)dy & 15) == 0 && ((uintptr_t)dtable & 15) == 0) {
-    const int64_t units = V * ((D / 4 + 31) / 32);
-    emb_sum4_kernel<<<grid_for(units * 32), 256, 0, s>>>(start, perm, dy, dtable, V, (int)(D / 4));
+    const int nseg = (int)emb_segments(rows, V, D);
+    float* part = reinterpret_cast<float*>(scratch + emb_head_ints(rows, V));
+    const int64_t units = V * ((D / 4 + 31) / 32) * nseg;
+    emb_sum4_kernel<<<grid_for(units * 32), 256, 0, s>>>(start, perm, dy, dtable, V, (int)(D / 4), nseg, part);
+    if (nseg > 1) emb_fold4_kernel<<<grid_for(V * D / 4), 256, 0, s>>>(part, dtable, V * D / 4, nseg);
     return;
   }
   int64_t cap = (int64_t)device_sm_count() * 16;

@@ -146,7 +146,7 @@ static int64_t scratch_for(const Program& P, int i, int action) {
     int a = P.op(i)["a"].i32();  // permute([K=V, rows])
     int64_t V = P.T[a].shape[0];
     int64_t rows = P.T[b].shape[0];
-    return (int64_t)embedding_grad_scratch_ints(rows, V) * 4;
+    return (int64_t)embedding_grad_scratch_ints(rows, V, P.T[b].shape[1]) * 4;
   }
   if (k == "sum_last" || k == "mean_last") {
     int a = P.op(i)["a"].i32();
