@@ -318,7 +318,6 @@ class Context {
   // worker rejects every pending request when the worker dies).
   void sync(cudaStream_t s);
   void check_comm() const;  // throws NcclError once the communicator was aborted
-  void abort_comm(const std::string& why);
   void allreduce_sum(float* buf, int64_t n, cudaStream_t s);
   // In-place sum allreduce of several ranges as one NCCL group.
   void allreduce_ranges(const std::vector<std::pair<float*, int64_t>>& ranges, cudaStream_t s);

@@ -6,7 +6,9 @@
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
+#include <atomic>
 #include <chrono>
+#include <memory>
 #include <set>
 #include <thread>
 
@@ -1724,12 +1726,6 @@ void Context::check_comm() const {
   if (nccl_aborted) throw TgError("NcclError", "the communicator was aborted after an earlier collective failure");
 }
 
-void Context::abort_comm(const std::string& why) {
-  if (nccl && !nccl_aborted) ncclCommAbort(reinterpret_cast<ncclComm_t>(nccl));
-  nccl_aborted = true;
-  throw TgError("NcclError", why + "; communicator aborted");
-}
-
 void Context::allreduce_ranges(const std::vector<std::pair<float*, int64_t>>& ranges, cudaStream_t s) {
   check_comm();
   ncclComm_t comm = reinterpret_cast<ncclComm_t>(nccl);
@@ -1747,6 +1743,23 @@ void Context::allreduce_sum(float* buf, int64_t n, cudaStream_t s) {
   ncclComm_t comm = reinterpret_cast<ncclComm_t>(nccl);
   ncclResult_t r = settle(comm, ncclAllReduce(buf, buf, (size_t)n, ncclFloat32, ncclSum, comm, s));
   if (r != ncclSuccess) throw TgError("NcclError", std::string("ncclAllReduce: ") + ncclGetErrorString(r));
+}
+
+// ncclCommAbort on a detached host thread, waited for at most timeout_s,
+// then a bounded wait for the stream: on this pool an abort issued by both
+// ranks of a communicator at once was seen not to return (NCCL 2.28.9), and a
+// failing step must still come back to its caller with an error.
+static void abort_bounded(ncclComm_t comm, cudaStream_t s, double timeout_s) {
+  auto done = std::make_shared<std::atomic<bool>>(false);
+  std::thread([comm, done] {
+    ncclCommAbort(comm);
+    done->store(true);
+  }).detach();
+  poll_until(timeout_s, [&] { return done->load() ? 0 : 1; });
+  poll_until(timeout_s, [&] {
+    const cudaError_t e = cudaStreamQuery(s);
+    return e == cudaErrorNotReady ? 1 : 0;
+  });
 }
 
 void Context::sync(cudaStream_t s) {
@@ -1780,16 +1793,14 @@ void Context::sync(cudaStream_t s) {
   if (w > 0) {
     // the step's work may still be queued behind a collective that waits on
     // a peer: abort it, then wait for the stream to drain
-    if (!nccl_aborted) ncclCommAbort(comm);
+    if (!nccl_aborted) abort_bounded(comm, s, to);
     nccl_aborted = true;
-    cudaStreamSynchronize(s);
     throw TgError("NcclError", "step did not complete within " + std::to_string(to) + " s" +
                                    (stall ? " (TG_FAULT=step_stall)" : " (a peer rank stalled or left)") +
                                    "; communicator aborted");
   }
-  if (!nccl_aborted) ncclCommAbort(comm);
+  if (!nccl_aborted) abort_bounded(comm, s, to);
   nccl_aborted = true;
-  cudaStreamSynchronize(s);
   throw TgError("NcclError", std::string("collective failed: ") + ncclGetErrorString(st) +
                                  (err ? " (TG_FAULT=step_error)" : "") + "; communicator aborted");
 }
