@@ -62,20 +62,22 @@ __device__ long long g_gemm_tc_trace[12][TC_TRACE_N];
 
 constexpr int TC_BM = 128, TC_BN = 128, TC_BK = 32;
 constexpr int TC_TILE_BYTES = 128 * TC_BK * 4;  // 16 KB per operand tile
-// Per stage: [0] A as landed by TMA, [1] B hi (K-major MMA operand; TMA lands
-// a K-major B here and it is split in place), [2] B lo, [3] B as landed when
-// it is MN-major. Three stages hide the TMA latency (1.5-2.5K cycles) plus the
-// split (about 1K); a fourth measured no faster. A K-major B needs no slot 3,
-// and the 48 KB saved hold the whole output tile for the epilogue (one
-// staging pass instead of two).
-#ifndef TC_STAGES_BK
-#define TC_STAGES_BK 3
-#define TC_EPI_BK 4
-#endif
-template <bool BK> struct TcCfg {
-  static constexpr int stages = BK ? TC_STAGES_BK : 3;
-  static constexpr int stage_bytes = (BK ? 3 : 4) * TC_TILE_BYTES;
-  static constexpr int epi_tiles = BK ? TC_EPI_BK : 2;  // 32 x 128 output sub-tiles staged at once
+// A stage holds `subs` 32-deep K sub-tiles of each operand: [A sub 0..][B hi
+// sub 0..] (K-major MMA operand; TMA lands a K-major B here and it is split in
+// place) [B lo sub 0..] and, when B is MN-major, [B as landed]. The issuing
+// thread's per-stage costs (barrier wait, fence, commits, the bubble before
+// the first MMA that reads freshly stored TMEM) are fixed, so large problems
+// with a K-major B (many tiles per SM) take 64-deep stages: 24 MMAs each, two
+// stages in flight. Otherwise three 32-deep stages: with few tiles per SM the
+// deeper ring's shorter fill wins (measured on C4's projections), and an
+// MN-major B needs its landing slot.
+template <bool BK, int SUBS> struct TcCfg {
+  static constexpr int subs = SUBS;
+  static constexpr int sk = TC_BK * subs;                 // K per stage
+  static constexpr int stages = (BK ? 3 : 4) * SUBS >= 6 ? 2 : 3;
+  static constexpr int stage_bytes = (BK ? 3 * subs : 4) * TC_TILE_BYTES;
+  static constexpr int epi_tiles = BK && SUBS == 1 ? 4 : 2;  // 32 x 128 output sub-tiles staged at once
+  static constexpr int chunk = 4 / subs;  // stages per accumulator chunk: 128 K either way
   static constexpr int ring_bytes = stages * stage_bytes;
   static constexpr int smem = ring_bytes + epi_tiles * TC_TILE_BYTES + 1024 + 256;
 };
@@ -100,6 +102,7 @@ struct TcParams {
   int trace;        // record the pipeline timeline of CTA (0,0,0)
   int tma_store;    // write the tile with TMA stores through tmC (else plain stores)
   int64_t units;    // output tiles x batch x K ranges
+  int sk;           // K per pipeline stage (TcCfg::sk of the launched kernel)
   int tri;          // GemmDesc::tri for the output rows (m tiles), or for the columns when
   int tri_n;        // tri_n (the operands were swapped); only without split-K
 };
@@ -196,13 +199,9 @@ __device__ __forceinline__ float tf32_hi(float x) { return __uint_as_float(__flo
 // Accumulator chunking: the tensor core accumulates in f32 without
 // round-to-nearest on every add, so error grows with the number of
 // accumulation steps. The MMA warp therefore alternates between two TMEM
-// accumulators every TC_CHUNK K-stages (128 MMA-K), and the epilogue warps
+// accumulators every 128 K (TcCfg::chunk stages), and the epilogue warps
 // drain each finished accumulator into per-thread f32 registers with
 // round-to-nearest adds; total error then grows like sqrt(K) instead of K.
-#ifndef TC_CHUNK_STAGES
-#define TC_CHUNK_STAGES 4
-#endif
-constexpr int TC_CHUNK = TC_CHUNK_STAGES;
 
 // One output tile of one batch entry and one K range: the persistent CTAs'
 // unit of work, numbered with the N tile fastest.
@@ -220,13 +219,13 @@ __device__ __forceinline__ TcUnit tc_unit(const TcParams& P, int64_t u) {
   U.sp = (int)(z % P.splits);
   U.i1 = (int)(U.zb / P.batch2);
   U.i2 = (int)(U.zb % P.batch2);
-  const int nk_all = (int)((P.K + TC_BK - 1) / TC_BK);
+  const int nk_all = (int)((P.K + P.sk - 1) / P.sk);
   U.kbeg = U.sp * P.kps;
   U.nk = max(0, min(nk_all, U.kbeg + P.kps) - U.kbeg);
   if (P.tri) {  // skip the K stages whose products are exactly zero (causal A)
     const int r0 = (int)(P.tri_n ? U.n0 : U.m0);
-    if (P.tri == 1) U.nk = min(nk_all, (r0 + TC_BM + TC_BK - 1) / TC_BK);
-    else { U.kbeg = r0 / TC_BK; U.nk = max(0, nk_all - U.kbeg); }
+    if (P.tri == 1) U.nk = min(nk_all, (r0 + TC_BM + P.sk - 1) / P.sk);
+    else { U.kbeg = r0 / P.sk; U.nk = max(0, nk_all - U.kbeg); }
   }
   return U;
 }
@@ -268,10 +267,9 @@ __device__ __forceinline__ void split_a_row(const uint8_t* a, int r, bool kmajor
   }
 }
 
-// B tile -> K-major hi (slot 1) and lo (slot 2) tiles, 128 threads.
-__device__ __forceinline__ void split_b(uint8_t* st, int t, bool kmajor) {
-  uint8_t* hi_t = st + TC_TILE_BYTES;
-  uint8_t* lo_t = st + 2 * TC_TILE_BYTES;
+// B tile -> K-major hi and lo tiles, 128 threads. A K-major B landed in
+// hi_t; an MN-major one landed in stg.
+__device__ __forceinline__ void split_b(uint8_t* hi_t, uint8_t* lo_t, const uint8_t* stg_in, int t, bool kmajor) {
   if (kmajor) {
     // Landed K-major in slot 1, which the MMA reads as hi unchanged: kind::tf32
     // MMAs ignore the low 13 mantissa bits of their f32 operands (truncation,
@@ -290,7 +288,7 @@ __device__ __forceinline__ void split_b(uint8_t* st, int t, bool kmajor) {
     // transpose, four 16-byte writes each to hi and lo, where element (n, k)
     // sits in row n, chunk (k/4) XOR (n%8). Lanes of a quarter-warp take two
     // N chunks x four K quads: the writes are conflict-free, the reads 2-way.
-    const uint8_t* stg = st + 3 * TC_TILE_BYTES;
+    const uint8_t* stg = stg_in;
     const int l8 = t & 7, q = (t >> 3) & 3, wq = t >> 5;
 #pragma unroll
     for (int it2 = 0; it2 < 2; ++it2) {
@@ -323,20 +321,23 @@ __device__ __forceinline__ void split_b(uint8_t* st, int t, bool kmajor) {
 // Persistent: each CTA walks units blockIdx.x, blockIdx.x + gridDim.x, ...;
 // the stage ring, the accumulator pair and every barrier phase continue
 // across units, so one unit's epilogue overlaps the next unit's main loop.
-template <bool BK>
+template <bool BK, int SUBS_>
 __global__ void __launch_bounds__(448, 1) gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA,
                                                          const __grid_constant__ CUtensorMap tmB,
                                                          const __grid_constant__ CUtensorMap tmC,
                                                          const __grid_constant__ TcParams P) {
-  constexpr int NS = TcCfg<BK>::stages;
-  constexpr int SB = TcCfg<BK>::stage_bytes;
-  constexpr int ET = TcCfg<BK>::epi_tiles;
+  constexpr int NS = TcCfg<BK, SUBS_>::stages;
+  constexpr int SB = TcCfg<BK, SUBS_>::stage_bytes;
+  constexpr int ET = TcCfg<BK, SUBS_>::epi_tiles;
+  constexpr int SUBS = SUBS_;
+  constexpr int CH = TcCfg<BK, SUBS_>::chunk;
+  constexpr int TB = TC_TILE_BYTES;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   // 1 KB-aligned base for the 128B-swizzled tiles. Offsetting the shared
   // array (rather than casting through an integer) keeps the pointer in the
   // shared address space, so tile accesses compile to shared loads/stores.
   uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
-  uint8_t* epi = smem + TcCfg<BK>::ring_bytes;  // ET output sub-tiles
+  uint8_t* epi = smem + TcCfg<BK, SUBS_>::ring_bytes;  // ET output sub-tiles
   uint64_t* full = reinterpret_cast<uint64_t*>(epi + ET * TC_TILE_BYTES);
   uint64_t* conv = full + NS;
   uint64_t* empty = conv + NS;
@@ -396,14 +397,18 @@ __global__ void __launch_bounds__(448, 1) gemm_tc_kernel(const __grid_constant__
           uint8_t* st = smem + s * SB;
           mark(0, gs);
           if (blockIdx.x == 0) g_gemm_tc_dbg[0] = gs + 1;
-          mbar_expect_tx(&full[s], 2 * TC_TILE_BYTES);
-          const int k0 = (U.kbeg + it) * TC_BK;
-          if (P.a_kmajor) tma_load_4d(&tmA, &full[s], st, k0, (int)U.m0, ab1, ab2);
-          else for (int j = 0; j < 4; ++j)
-            tma_load_4d(&tmA, &full[s], st + j * 4096, (int)U.m0 + 32 * j, k0, ab1, ab2);
-          if (P.b_kmajor) tma_load_4d(&tmB, &full[s], st + TC_TILE_BYTES, k0, (int)U.n0, bb1, bb2);
-          else for (int j = 0; j < 4; ++j)
-            tma_load_4d(&tmB, &full[s], st + 3 * TC_TILE_BYTES + j * 4096, (int)U.n0 + 32 * j, k0, bb1, bb2);
+          mbar_expect_tx(&full[s], 2 * SUBS * TB);
+#pragma unroll
+          for (int q = 0; q < SUBS; ++q) {
+            const int k0 = (U.kbeg + it) * TcCfg<BK, SUBS_>::sk + TC_BK * q;
+            uint8_t* sa = st + q * TB;
+            if (P.a_kmajor) tma_load_4d(&tmA, &full[s], sa, k0, (int)U.m0, ab1, ab2);
+            else for (int j = 0; j < 4; ++j)
+              tma_load_4d(&tmA, &full[s], sa + j * 4096, (int)U.m0 + 32 * j, k0, ab1, ab2);
+            if (BK) tma_load_4d(&tmB, &full[s], st + (SUBS + q) * TB, k0, (int)U.n0, bb1, bb2);
+            else for (int j = 0; j < 4; ++j)
+              tma_load_4d(&tmB, &full[s], st + 3 * TB + j * 4096, (int)U.n0 + 32 * j, k0, bb1, bb2);
+          }
         }
       }
     }
@@ -418,7 +423,7 @@ __global__ void __launch_bounds__(448, 1) gemm_tc_kernel(const __grid_constant__
       // MMA queue is about one instruction deep), so the loop keeps only the
       // barrier wait, 12 MMAs and the commits. Shared-memory descriptors
       // advance by address >> 4 in their low field (smem < 256 KB, no carry).
-      const uint64_t desc0 = umma_desc(smem_u32(smem) + TC_TILE_BYTES, 16, 1024);
+      const uint64_t desc0 = umma_desc(smem_u32(smem) + SUBS * TB, 16, 1024);  // B hi, stage 0, sub 0
       const uint32_t a0 = tmem + TC_ACOL;
       int s = 0, gs = 0;
       uint32_t ph = 0;
@@ -426,33 +431,38 @@ __global__ void __launch_bounds__(448, 1) gemm_tc_kernel(const __grid_constant__
       for (int64_t u = blockIdx.x; u < P.units && ok; u += gridDim.x) {
         const TcUnit U = tc_unit(P, u);
         for (int it = 0; it < U.nk; ++it, ++gs) {
-          const int c = gc + it / TC_CHUNK, acc = c & 1;
-          const bool chunk_start = (it % TC_CHUNK) == 0;
+          const int c = gc + it / CH, acc = c & 1;
+          const bool chunk_start = (it % CH) == 0;
           if (chunk_start && c >= 2 && !mbar_wait(&dempty[acc], (uint32_t)((c - 2) >> 1) & 1u, 5)) {
             ok = false; break;
           }
           if (!mbar_wait(&conv[s], ph, 2)) { ok = false; break; }
           mark(10, gs);
           asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-          const uint64_t dh = desc0 + (uint64_t)(s * (SB >> 4)), dl = dh + (TC_TILE_BYTES >> 4);
-          const uint32_t a_hi = a0 + 64u * (uint32_t)s, a_lo = a_hi + 32u;
+          const uint64_t dh0 = desc0 + (uint64_t)(s * (SB >> 4));
+          const uint32_t a_s = a0 + 64u * SUBS * (uint32_t)s;
           const uint32_t dacc = tmem + (uint32_t)(acc * TC_BN);
 #pragma unroll
-          for (int kk = 0; kk < TC_BK / 8; ++kk) {
-            // B: 128 rows of 128 bytes (32 K values), 8-row groups 1 KB apart
-            // (SBO); a K step of 8 advances 32 bytes (2 in the address field).
-            // A: 8 TMEM columns.
-            const uint32_t first = (chunk_start && kk == 0) ? 0u : 1u;
-            umma_tf32_ts(dacc, a_lo + kk * 8, dh + 2 * kk, idesc, first);
-            umma_tf32_ts(dacc, a_hi + kk * 8, dl + 2 * kk, idesc, 1u);
-            umma_tf32_ts(dacc, a_hi + kk * 8, dh + 2 * kk, idesc, 1u);
+          for (int q = 0; q < SUBS; ++q) {
+            const uint64_t dh = dh0 + (uint64_t)(q * (TB >> 4)), dl = dh + (uint64_t)(SUBS * (TB >> 4));
+            const uint32_t a_hi = a_s + 64u * q, a_lo = a_hi + 32u;
+#pragma unroll
+            for (int kk = 0; kk < TC_BK / 8; ++kk) {
+              // B: 128 rows of 128 bytes (32 K values), 8-row groups 1 KB apart
+              // (SBO); a K step of 8 advances 32 bytes (2 in the address field).
+              // A: 8 TMEM columns.
+              const uint32_t first = (chunk_start && q == 0 && kk == 0) ? 0u : 1u;
+              umma_tf32_ts(dacc, a_lo + kk * 8, dh + 2 * kk, idesc, first);
+              umma_tf32_ts(dacc, a_hi + kk * 8, dl + 2 * kk, idesc, 1u);
+              umma_tf32_ts(dacc, a_hi + kk * 8, dh + 2 * kk, idesc, 1u);
+            }
           }
           mark(3, gs);
           umma_commit(&empty[s]);  // frees the stage (smem and TMEM A) once these MMAs have read it
-          if ((it % TC_CHUNK) == TC_CHUNK - 1 || it == U.nk - 1) umma_commit(&dfull[acc]);
+          if ((it % CH) == CH - 1 || it == U.nk - 1) umma_commit(&dfull[acc]);
           if (++s == NS) { s = 0; ph ^= 1u; }
         }
-        gc += (U.nk + TC_CHUNK - 1) / TC_CHUNK;
+        gc += (U.nk + CH - 1) / CH;
       }
     }
   } else if (warp < 6) {
@@ -472,8 +482,11 @@ __global__ void __launch_bounds__(448, 1) gemm_tc_kernel(const __grid_constant__
         if (t == 0) mark(1, gs);
         uint8_t* st = smem + s * SB;
         if (ok) {
-          split_a_row(st, r, P.a_kmajor != 0, tmem + lane_base + TC_ACOL + 64u * (uint32_t)s);
-          split_b(st, t, P.b_kmajor != 0);
+#pragma unroll
+          for (int q = 0; q < SUBS; ++q) {
+            split_a_row(st + q * TB, r, P.a_kmajor != 0, tmem + lane_base + TC_ACOL + 64u * (SUBS * (uint32_t)s + q));
+            split_b(st + (SUBS + q) * TB, st + (2 * SUBS + q) * TB, st + 3 * TB, t, BK);
+          }
         }
         asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
@@ -507,7 +520,7 @@ __global__ void __launch_bounds__(448, 1) gemm_tc_kernel(const __grid_constant__
     int gc = 0;
     for (int64_t u = blockIdx.x; u < P.units; u += gridDim.x) {
       const TcUnit U = tc_unit(P, u);
-      const int nchunks = (U.nk + TC_CHUNK - 1) / TC_CHUNK;
+      const int nchunks = (U.nk + CH - 1) / CH;
       float sum[64];
 #pragma unroll
       for (int j = 0; j < 64; ++j) sum[j] = 0.f;
@@ -746,7 +759,11 @@ bool launch_gemm_tc(const GemmDesc& g, cudaStream_t s) {
   p.b_b1 = b_b ? 1 : 0; p.b_b2 = b_b2 ? 1 : 0;
   p.C = g.C; p.c_m = c_m; p.c_n = c_n; p.c_batch = g.c_batch; p.c_batch2 = g.c_batch2;
   p.bias = g.bias; p.bias_m = swap ? 1 : 0; p.alpha = g.alpha; p.accumulate = g.accumulate;
-  const int64_t nk = (g.K + TC_BK - 1) / TC_BK;
+  // 64-deep stages for a K-major B when every SM has many tiles to run
+  const int64_t tiles_all = ((N + TC_BN - 1) / TC_BN) * ((M + TC_BM - 1) / TC_BM) * g.batch;
+  const bool deep = bk && tiles_all >= 8 * device_sm_count() && g.K >= 512;
+  p.sk = deep ? TcCfg<true, 2>::sk : TC_BK;
+  const int64_t nk = (g.K + p.sk - 1) / p.sk;
   int splits = gemm_tc_splits(M, N, g.K, g.batch);
   if (splits > 1 && (!g.workspace || g.workspace_floats < (int64_t)splits * g.batch * M * N)) splits = 1;
   p.kps = (int)((nk + splits - 1) / splits);
@@ -776,18 +793,21 @@ bool launch_gemm_tc(const GemmDesc& g, cudaStream_t s) {
 
   static bool attr = false;
   if (!attr) {
-    if (cudaFuncSetAttribute(gemm_tc_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             TcCfg<true>::smem) != cudaSuccess ||
-        cudaFuncSetAttribute(gemm_tc_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             TcCfg<false>::smem) != cudaSuccess)
+    if (cudaFuncSetAttribute(gemm_tc_kernel<true, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             TcCfg<true, 1>::smem) != cudaSuccess ||
+        cudaFuncSetAttribute(gemm_tc_kernel<true, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             TcCfg<true, 2>::smem) != cudaSuccess ||
+        cudaFuncSetAttribute(gemm_tc_kernel<false, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             TcCfg<false, 1>::smem) != cudaSuccess)
       return false;
     attr = true;
   }
   p.units = ((N + TC_BN - 1) / TC_BN) * ((M + TC_BM - 1) / TC_BM) * g.batch * splits;
   const int64_t sms = device_sm_count();
   const unsigned grid = (unsigned)(p.units < sms ? p.units : sms);
-  if (bk) gemm_tc_kernel<true><<<grid, 448, TcCfg<true>::smem, s>>>(ta, tb, tc, p);
-  else gemm_tc_kernel<false><<<grid, 448, TcCfg<false>::smem, s>>>(ta, tb, tc, p);
+  if (deep) gemm_tc_kernel<true, 2><<<grid, 448, TcCfg<true, 2>::smem, s>>>(ta, tb, tc, p);
+  else if (bk) gemm_tc_kernel<true, 1><<<grid, 448, TcCfg<true, 1>::smem, s>>>(ta, tb, tc, p);
+  else gemm_tc_kernel<false, 1><<<grid, 448, TcCfg<false, 1>::smem, s>>>(ta, tb, tc, p);
   if (splits > 1) {
     int64_t total = g.batch * M * N;
     int64_t blocks = (total + 255) / 256, cap = (int64_t)device_sm_count() * 8;
