@@ -639,11 +639,30 @@ __global__ void __launch_bounds__(256) gemm_splitk_reduce(const __grid_constant_
   const int64_t stride = (int64_t)gridDim.x * blockDim.x;
   const bool rowfast = P.c_m == 1 && P.c_n != 1;
   for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < total; e += stride) {
-    const int64_t zb = e / per, rem = e % per;
-    const int64_t row = rowfast ? rem % P.M : rem / P.N, col = rowfast ? rem / P.M : rem % P.N;
+    int64_t zb, row, col;
+    if (total <= INT32_MAX) {  // 32-bit index arithmetic (64-bit division is slow)
+      const uint32_t e32 = (uint32_t)e, per32 = (uint32_t)per, rem = e32 % per32;
+      zb = e32 / per32;
+      row = rowfast ? rem % (uint32_t)P.M : rem / (uint32_t)P.N;
+      col = rowfast ? rem / (uint32_t)P.M : rem % (uint32_t)P.N;
+    } else {
+      const int64_t rem = e % per;
+      zb = e / per;
+      row = rowfast ? rem % P.M : rem / P.N;
+      col = rowfast ? rem / P.M : rem % P.N;
+    }
     const int64_t w = zb * per + row * P.N + col;
+    // partials added in split order; eight loads in flight before their adds
     float v = 0.f;
-    for (int sp = 0; sp < P.splits; ++sp) v += P.ws[(int64_t)sp * total + w];
+    int sp = 0;
+    for (; sp + 8 <= P.splits; sp += 8) {
+      float x[8];
+#pragma unroll
+      for (int q = 0; q < 8; ++q) x[q] = __ldg(P.ws + (int64_t)(sp + q) * total + w);
+#pragma unroll
+      for (int q = 0; q < 8; ++q) v += x[q];
+    }
+    for (; sp < P.splits; ++sp) v += __ldg(P.ws + (int64_t)sp * total + w);
     v = __fmul_rn(v, P.alpha);
     if (P.bias) v += P.bias[P.bias_m ? row : col];
     const int64_t i1 = zb / P.batch2, i2 = zb % P.batch2;
