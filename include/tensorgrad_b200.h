@@ -128,8 +128,10 @@ int tg_profile_step(tg_ctx* ctx, int graph_id, float* ms_out, int cap, int* n_ou
  * each memory-bound kernel's achieved bandwidth. (new: measurement) */
 int tg_launch_bytes(tg_ctx* ctx, int graph_id, double* out, int cap, int* n_out);
 
-/* Error code recorded by a tcgen05 GEMM whose bounded barrier wait ran out
- * (0 = none); reset != 0 clears it. (new: kernel health check for tests) */
+/* Error code recorded by a tcgen05 kernel whose bounded barrier wait ran out
+ * (0 = none): the GEMM's code in the low byte, the attention forward's
+ * shifted left by 8; reset != 0 clears both. (new: kernel health check for
+ * tests) */
 int tg_debug_gemm_error(int reset);
 /* Progress markers of the first GEMM tile (8 ints) for pipeline diagnosis. */
 int tg_debug_gemm_dbg(int* out8);

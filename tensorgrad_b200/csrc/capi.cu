@@ -275,7 +275,9 @@ int tg_launch_bytes(tg_ctx* ctx, int graph_id, double* out, int cap, int* n_out)
   });
 }
 
-int tg_debug_gemm_error(int reset) { return tg::gemm_tc_error_flag(reset != 0); }
+int tg_debug_gemm_error(int reset) {
+  return tg::gemm_tc_error_flag(reset != 0) | (tg::attn_tc_error_flag(reset != 0) << 8);
+}
 int tg_debug_gemm_dbg(int* out8) { return tg::gemm_tc_debug(out8); }
 int tg_debug_gemm_trace(long long* out, int cap) { return tg::gemm_tc_trace(out, cap); }
 

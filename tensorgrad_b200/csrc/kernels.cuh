@@ -156,6 +156,11 @@ struct AttnParams {
 };
 bool attn_supported_dim(int d);
 void launch_attn_fwd(const AttnParams& P, cudaStream_t s);
+// tcgen05 forward (head dim 64, no dropout, unit head-dim stride; opt-in with
+// TG_ATTN_TC=1); false when the block is not taken (the warp-MMA forward runs
+// instead).
+bool launch_attn_fwd_tc(const AttnParams& P, cudaStream_t s);
+int attn_tc_error_flag(bool reset);
 void launch_attn_bwd(const AttnParams& P, cudaStream_t s);
 // Row-strided copy to a new row stride (operand staging for TMA).
 void launch_pad_rows(const float* src, int64_t ld_src, float* dst, int64_t ld_dst, int64_t rows, int64_t cols,

@@ -487,6 +487,7 @@ static void attn_bwd_t(const AttnParams& P, cudaStream_t s) {
 bool attn_supported_dim(int d) { return d == 16 || d == 32 || d == 64; }
 
 void launch_attn_fwd(const AttnParams& P, cudaStream_t s) {
+  if (launch_attn_fwd_tc(P, s)) return;
   if (P.D == 64) attn_fwd_t<64>(P, s);
   else if (P.D == 32) attn_fwd_t<32>(P, s);
   else attn_fwd_t<16>(P, s);

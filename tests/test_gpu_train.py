@@ -113,12 +113,15 @@ def test_train_parity(ctx, name, steps=5):
     dict(T=200, D=128, heads=2, layers=1, batch=2, dropout=0.2),  # head dim 64, ragged last block
     dict(T=128, D=128, heads=2, layers=1, batch=2, dropout=0.0),  # no dropout op in the chain
     dict(T=96, D=64, heads=2, layers=2, batch=3, dropout=0.2),    # head dim 32
+    dict(T=300, D=128, heads=2, layers=1, batch=2, dropout=0.0),  # tcgen05 forward, ragged last block
 ])
 def test_fused_attention_train_parity(ctx, over, monkeypatch):
     """GPT steps whose attention runs as the fused flash-style kernels
     (forward, and dK/dV/dS plus dQ backward) against the oracle's unfused
-    graph: loss, every gradient and the optimizer update."""
+    graph: loss, every gradient and the optimizer update. TG_ATTN_TC=1 puts
+    the dropout-free head-dim-64 cases on the tcgen05 forward."""
     monkeypatch.setenv("TG_ATTN_FUSE", "1")
+    monkeypatch.setenv("TG_ATTN_TC", "1")
     _parity(ctx, "c4", 2, **over)
 
 
